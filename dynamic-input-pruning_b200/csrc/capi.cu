@@ -1,0 +1,88 @@
+// capi.cu — library-wide entry points: status handling, PDL switch and the
+// whole-layer decode chain (StreamingDIPMlp.forward,
+// dip_stream_predispatch.py:176-204, with the PCIe staging removed because
+// every weight is resident in HBM).
+#include <atomic>
+#include <cstring>
+
+#include "dip_common.cuh"
+
+namespace dip {
+
+static std::atomic<int> g_pdl{1};
+static thread_local char g_last_err[256] = "";
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+int launch_status(cudaError_t e) {
+  if (e == cudaSuccess) return DIP_OK;
+  std::strncpy(g_last_err, cudaGetErrorString(e), sizeof(g_last_err) - 1);
+  return DIP_ERR_CUDA;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n;
+}
+
+size_t down_workspace_bytes(int64_t out);
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace dip
+
+using namespace dip;
+
+extern "C" int dip_version(void) { return 100; }
+
+extern "C" const char* dip_status_string(int status) {
+  switch (status) {
+    case DIP_OK: return "ok";
+    case DIP_ERR_ARG: return "invalid argument (null pointer, size or alignment)";
+    case DIP_ERR_CUDA: return "CUDA error";
+    case DIP_ERR_WORKSPACE: return "workspace too small";
+    case DIP_ERR_UNSUPPORTED: return "unsupported shape";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* dip_last_cuda_error(void) { return g_last_err; }
+
+extern "C" int dip_set_pdl(int enable) { return g_pdl.exchange(enable ? 1 : 0); }
+
+extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
+  if (hidden <= 0 || inter <= 0 || k < 0) return 0;
+  return align256((size_t)inter * 2) + align256((size_t)k * 4) + align256((size_t)k * 2) +
+         align256(down_workspace_bytes(hidden));
+}
+
+extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k, void* workspace,
+                              size_t workspace_bytes, dip_bf16* y, dip_bf16* g_out,
+                              int32_t* idx_out, dip_stream_t stream) {
+  if (!L || !x || !y || !workspace) return DIP_ERR_ARG;
+  if (k < 1 || k > L->inter) return DIP_ERR_ARG;
+  const size_t need = dip_mlp_workspace_bytes(L->hidden, L->inter, k);
+  if (need == 0) return DIP_ERR_ARG;
+  if (workspace_bytes < need) return DIP_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  dip_bf16* g = reinterpret_cast<dip_bf16*>(ws);
+  ws += align256((size_t)L->inter * 2);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws);
+  ws += align256((size_t)k * 4);
+  dip_bf16* h = reinterpret_cast<dip_bf16*>(ws);
+  ws += align256((size_t)k * 2);
+  void* part = ws;
+  const size_t part_bytes = workspace_bytes - (size_t)(ws - static_cast<uint8_t*>(workspace));
+  if (g_out) g = g_out;
+  if (idx_out) idx = idx_out;
+
+  int st = dip_int4_gemv(L->gate_qw, L->gate_sc, x, g, L->inter, L->hidden, 1, stream);
+  if (st) return st;
+  st = dip_topk_select(g, L->inter, k, idx, stream);
+  if (st) return st;
+  st = dip_gather_up_h(L->up_qw, L->up_sc, L->inter, x, g, idx, k, L->hidden, h, stream);
+  if (st) return st;
+  return dip_int4_gather_down(L->down_t_qw, L->down_t_sc, L->inter, h, idx, k, L->hidden, part,
+                              part_bytes, y, stream);
+}

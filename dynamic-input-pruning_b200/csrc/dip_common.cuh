@@ -1,0 +1,117 @@
+// dip_common.cuh — shared device helpers for the sm_100a DIP kernels.
+//
+// Weight format (identical to the reference's, scripts/quantize.py:32-64 and
+// qlinear.py:28-64): a row of `in` int4 values is `in/2` bytes, two signed
+// (two's complement) nibbles per byte, low nibble = even column; one bf16
+// scale per 128 consecutive columns.  w = q * s.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "../../include/dip_b200.h"
+
+namespace dip {
+
+constexpr int kGroup = 128;          // quantisation group (columns per scale)
+constexpr int kGroupBytes = kGroup / 2;
+
+// ---------------------------------------------------------------------------
+// bf16 <-> float on raw 16-bit patterns (the C-ABI passes bf16 as uint16_t).
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) {
+  return __uint_as_float(b << 16);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  __nv_bfloat16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_bits_to_f32(f32_to_bf16_bits(f));
+}
+
+// ---------------------------------------------------------------------------
+// int4 -> bf16 in-register conversion (the "magic number" technique: place
+// an integer in the low mantissa bits of a float whose exponent makes the
+// mantissa step exactly 1, here bf16 128.0 = 0x4300).  The nibble is stored
+// in two's complement; XOR with 8 turns it into offset binary, so each
+// 16-bit lane below holds exactly  128 + (q + 8) = q + 136  with q in [-8,7].
+// Lane pairing: out[p] = (nibble p, nibble p+4) for p = 0..3.
+constexpr float kNibbleBias = 136.0f;
+__device__ __forceinline__ void nib8_biased_bf16x2(uint32_t w, uint32_t (&o)[4]) {
+  o[0] = (w & 0x000F000Fu) ^ 0x43084308u;
+  o[1] = ((w >> 4) & 0x000F000Fu) ^ 0x43084308u;
+  o[2] = ((w >> 8) & 0x000F000Fu) ^ 0x43084308u;
+  o[3] = ((w >> 12) & 0x000F000Fu) ^ 0x43084308u;
+}
+
+// Same idea in fp32: 2^23 = 0x4B000000 has a mantissa step of 1, so
+// (nibble bits << 4j) | 0x4B000000 == 2^23 + u*16^j exactly for bit
+// positions below 23.
+constexpr uint32_t kF32Magic = 0x4B000000u;
+
+// Warp-level MMA m16n8k16, bf16 x bf16 -> fp32 (legacy tensor path; used as
+// the multiply-accumulate engine of the batch-1 GEMVs).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Streaming 128-bit load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) {
+  return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+// Programmatic dependent launch (PDL).  A kernel launched with the
+// programmatic-serialisation attribute may start before its predecessor
+// finishes; it must call pdl_wait() before touching the predecessor's
+// outputs.  pdl_launch_dependents() lets the successor start early.  Both are
+// no-ops when the kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+__device__ __forceinline__ float silu_f32(float v) {
+  return v / (1.0f + expf(-v));
+}
+
+// ---------------------------------------------------------------------------
+// Host side helpers.
+int launch_status(cudaError_t e);
+
+// Whether kernels launched through the C-ABI use programmatic dependent
+// launch (set with dip_set_pdl; default on).
+bool pdl_enabled();
+
+template <typename Kernel, typename... Args>
+cudaError_t launch(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+int num_sms();
+
+}  // namespace dip

@@ -1,0 +1,367 @@
+// gemv_int4.cu — batch-1 int4 (g128) GEMV family for sm_100a.
+//
+// One kernel serves four reference operations, selected by template
+// parameters:
+//   * dense rows           -> int4_ops::int4_gemv (+ fused SiLU)
+//                             reference: kernels/int4_gemv/int4_gemv.cu:39-108
+//   * rows gathered by idx -> int4_gather_ops::int4_gather_gemv
+//                             reference: kernels/int4_gather/int4_gather_gemv.cu:39-108
+//   * (src,row) dual source-> ca_fused_ops::ca_fused_gemv
+//                             reference: kernels/ca_fused/ca_fused_gemv.cu:44-105
+//   * optional epilogue h = bf16(g[c] * bf16(u))  (dip_stream_predispatch.py:201)
+//
+// Design.  A CTA of 4 warps owns a tile of 16 output rows; warp w handles
+// the quantisation groups w, w+4, w+8, ... of every row, so the 4 warps read
+// 256 contiguous bytes of each row at a time.  Lane (g = lane/4, t = lane%4)
+// loads 16 B (32 nibbles) of rows g and g+8 per group with one 128-bit
+// non-allocating load each.  Nibbles become bf16 values q+136 in registers
+// (magic-number conversion, 7 integer ops per 8 nibbles, no conversion
+// instructions) and feed mma.sync m16n8k16 with fp32 accumulation: the tensor
+// core performs the multiply-adds and the cross-lane reduction that a
+// CUDA-core GEMV spends most of its issue slots on.  x is staged once per CTA
+// in shared memory, permuted so that each lane's B fragment is 4 LDS.128.
+// The constant bias 136 is removed per group with the group sum of x:
+//   sum_k (q+136) x = sum_k q x + 136 * sum_k x.
+// Each group's partial is scaled by its bf16 scale in fp32, and the 4 warps'
+// partials are summed in a fixed order (deterministic).
+#include "dip_common.cuh"
+
+namespace dip {
+
+enum RowMode : int { ROW_DENSE = 0, ROW_GATHER = 1, ROW_SRCROW = 2 };
+enum Epilogue : int { EPI_PLAIN = 0, EPI_SILU = 1, EPI_H = 2 };
+
+struct GemvParams {
+  const uint8_t* qw0;  // source 0 rows [n0, in/2]
+  const uint16_t* sc0; // source 0 scales [n0, in/128]
+  int64_t n0;
+  const uint8_t* qw1;  // source 1 (ROW_SRCROW, src == 1)
+  const uint16_t* sc1;
+  int64_t n1;
+  const uint16_t* x;   // [in]
+  const int32_t* idx;  // ROW_GATHER: row of output j
+  const int32_t* src;  // ROW_SRCROW: source of output j
+  const int32_t* row;  // ROW_SRCROW: row within that source
+  const uint16_t* g;   // EPI_H: gate activations by channel id
+  const int32_t* gid;  // EPI_H: channel id of output j
+  uint16_t* out;       // [n_out]
+  int n_out;
+  int in_features;
+};
+
+constexpr int kGemvWarps = 4;
+constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr int kGemvBatch = 5;  // groups whose loads are in flight per warp
+
+template <int MODE>
+__device__ __forceinline__ bool resolve_row(const GemvParams& p, int j, const uint8_t*& qw,
+                                            const uint16_t*& sc) {
+  const int64_t rb = p.in_features / 2;
+  const int64_t sb = p.in_features / kGroup;
+  int64_t r;
+  int s = 0;
+  if (MODE == ROW_DENSE) {
+    r = j;
+  } else if (MODE == ROW_GATHER) {
+    r = p.idx[j];
+  } else {
+    s = p.src[j];
+    r = p.row[j];
+  }
+  const int64_t n = (s == 0) ? p.n0 : p.n1;
+  const bool ok = (s == 0 || s == 1) && r >= 0 && r < n;
+  if (!ok) r = 0;
+  const uint8_t* q = (s == 0) ? p.qw0 : p.qw1;
+  const uint16_t* c = (s == 0) ? p.sc0 : p.sc1;
+  if (!ok) { q = p.qw0; c = p.sc0; }
+  qw = q + r * rb;
+  sc = c + r * sb;
+  return ok;
+}
+
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_int4_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int in = p.in_features;
+  const int G = in / kGroup;
+  uint32_t* xperm = reinterpret_cast<uint32_t*>(smem_raw);              // in/2 words
+  float* gsum = reinterpret_cast<float*>(smem_raw + (size_t)in * 2);    // G
+  float* red = gsum + G;                                                // [4][16]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gq = lane >> 2;  // fragment row group
+  const int tq = lane & 3;   // fragment column quad
+  const int tile0 = blockIdx.x * 16;
+
+  // Rows of this lane: tile0+gq and tile0+gq+8 (clamped for the last tile).
+  const int ja = min(tile0 + gq, p.n_out - 1);
+  const int jb = min(tile0 + gq + 8, p.n_out - 1);
+
+  // Row indices of gathered modes come from the previous kernel.
+  if (MODE != ROW_DENSE) pdl_wait();
+  const uint8_t *qa, *qb;
+  const uint16_t *sa_p, *sb_p;
+  const bool oka = resolve_row<MODE>(p, ja, qa, sa_p);
+  const bool okb = resolve_row<MODE>(p, jb, qb, sb_p);
+
+  // First batch of weight loads is issued before waiting on the predecessor
+  // (weights are never written by it).
+  uint4 wa[kGemvBatch], wb[kGemvBatch];
+  float sa[kGemvBatch], sbv[kGemvBatch];
+  auto load_batch = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < kGemvBatch; ++u) {
+      const int grp = base + kGemvWarps * u;
+      if (grp < G) {
+        const int off = grp * kGroupBytes + tq * 16;
+        wa[u] = ldg_stream_u4(qa + off);
+        wb[u] = ldg_stream_u4(qb + off);
+        sa[u] = bf16_bits_to_f32(ldg_u16(sa_p + grp));
+        sbv[u] = bf16_bits_to_f32(ldg_u16(sb_p + grp));
+      }
+    }
+  };
+  load_batch(warp);
+  if (MODE == ROW_DENSE) pdl_wait();
+
+  // Stage x: each 8-column word (x0..x7) is stored as
+  // [(x0,x4),(x1,x5),(x2,x6),(x3,x7)] which is the B-fragment order matching
+  // the nibble pairing of nib8_biased_bf16x2; also the per-group sums of x.
+  {
+    const int nwords = in / 8;
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+    for (int wi = threadIdx.x; wi < ((nwords + 127) & ~127); wi += kGemvThreads) {
+      float part = 0.f;
+      if (wi < nwords) {
+        const uint4 v = __ldg(xv + wi);
+        uint4 o;
+        o.x = __byte_perm(v.x, v.z, 0x5410);
+        o.y = __byte_perm(v.x, v.z, 0x7632);
+        o.z = __byte_perm(v.y, v.w, 0x5410);
+        o.w = __byte_perm(v.y, v.w, 0x7632);
+        reinterpret_cast<uint4*>(xperm)[wi] = o;
+        part = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) +
+               bf16_bits_to_f32(v.y & 0xFFFF) + bf16_bits_to_f32(v.y >> 16) +
+               bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
+               bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
+      }
+      // 16 consecutive words form one group; they sit in 16 consecutive lanes.
+      part += __shfl_xor_sync(0xffffffffu, part, 8);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
+    }
+  }
+  __syncthreads();
+
+  float acc_a = 0.f, acc_b = 0.f;
+  for (int base = warp; base < G; base += kGemvWarps * kGemvBatch) {
+    if (base != warp) load_batch(base);
+#pragma unroll
+    for (int u = 0; u < kGemvBatch; ++u) {
+      const int grp = base + kGemvWarps * u;
+      if (grp < G) {
+        const uint4* bp = reinterpret_cast<const uint4*>(xperm + grp * 64 + tq * 16);
+        const uint4 b01 = bp[0], b23 = bp[1], b45 = bp[2], b67 = bp[3];
+        const uint32_t bw[16] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w,
+                                 b45.x, b45.y, b45.z, b45.w, b67.x, b67.y, b67.z, b67.w};
+        const uint32_t ra[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+        const uint32_t rb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+        float d0[4] = {0.f, 0.f, 0.f, 0.f};
+        float d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint32_t qa4[4], qb4[4];
+          nib8_biased_bf16x2(ra[w], qa4);
+          nib8_biased_bf16x2(rb[w], qb4);
+          const uint32_t a_even[4] = {qa4[0], qb4[0], qa4[1], qb4[1]};
+          const uint32_t a_odd[4] = {qa4[2], qb4[2], qa4[3], qb4[3]};
+          mma_bf16_16816(d0, a_even, bw[4 * w + 0], bw[4 * w + 1]);
+          mma_bf16_16816(d1, a_odd, bw[4 * w + 2], bw[4 * w + 3]);
+        }
+        const float bias = kNibbleBias * gsum[grp];
+        acc_a = fmaf(sa[u], (d0[0] + d1[0]) - bias, acc_a);
+        acc_b = fmaf(sbv[u], (d0[2] + d1[2]) - bias, acc_b);
+      }
+    }
+  }
+  pdl_launch_dependents();
+
+  if (tq == 0) {
+    red[warp * 16 + gq] = acc_a;
+    red[warp * 16 + gq + 8] = acc_b;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    const int j = tile0 + threadIdx.x;
+    if (j < p.n_out) {
+      float v = red[threadIdx.x];
+#pragma unroll
+      for (int w = 1; w < kGemvWarps; ++w) v += red[w * 16 + threadIdx.x];
+      const bool ok = (threadIdx.x < 8) ? oka : okb;
+      uint16_t o;
+      if (!ok) {
+        o = 0;
+      } else if (EPI == EPI_PLAIN) {
+        o = f32_to_bf16_bits(v);
+      } else if (EPI == EPI_SILU) {
+        o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+      } else {
+        const float u = round_bf16(v);
+        const float gv = bf16_bits_to_f32(p.g[p.gid[j]]);
+        o = f32_to_bf16_bits(gv * u);
+      }
+      p.out[j] = o;
+    }
+  }
+}
+
+// Host launcher shared by the entry points below.
+template <int MODE, int EPI>
+static int launch_gemv(const GemvParams& p, cudaStream_t s) {
+  if (p.n_out == 0) return DIP_OK;
+  const int G = p.in_features / kGroup;
+  const size_t smem = (size_t)p.in_features * 2 + (size_t)G * 4 + kGemvWarps * 16 * 4;
+  auto kern = gemv_int4_kernel<MODE, EPI>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return launch_status(e);
+  }
+  const dim3 grid((p.n_out + 15) / 16);
+  return launch_status(launch(kern, grid, dim3(kGemvThreads), smem, s, p));
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static bool gemv_shape_ok(int64_t in_features) {
+  return in_features > 0 && in_features % kGroup == 0 && in_features <= 65536;
+}
+
+}  // namespace dip
+
+using namespace dip;
+
+extern "C" int dip_int4_gemv(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
+                             dip_bf16* out, int64_t rows, int64_t in_features, int apply_silu,
+                             dip_stream_t stream) {
+  if (rows < 0 || rows > INT32_MAX || !gemv_shape_ok(in_features)) return DIP_ERR_ARG;
+  if (rows == 0) return DIP_OK;
+  if (!qweight || !scales || !x || !out || !aligned16(qweight) || !aligned16(x))
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(qweight);
+  p.sc0 = scales;
+  p.n0 = rows;
+  p.x = x;
+  p.out = out;
+  p.n_out = (int)rows;
+  p.in_features = (int)in_features;
+  return apply_silu ? launch_gemv<ROW_DENSE, EPI_SILU>(p, (cudaStream_t)stream)
+                    : launch_gemv<ROW_DENSE, EPI_PLAIN>(p, (cudaStream_t)stream);
+}
+
+extern "C" int dip_int4_gather_gemv(const int8_t* qweight, const dip_bf16* scales,
+                                    int64_t n_rows, const dip_bf16* x, const int32_t* indices,
+                                    int64_t k, int64_t in_features, dip_bf16* out,
+                                    dip_stream_t stream) {
+  if (k < 0 || k > INT32_MAX || n_rows < 0 || !gemv_shape_ok(in_features)) return DIP_ERR_ARG;
+  if (k == 0) return DIP_OK;
+  if (!qweight || !scales || !x || !indices || !out || n_rows == 0 || !aligned16(qweight) ||
+      !aligned16(x))
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(qweight);
+  p.sc0 = scales;
+  p.n0 = n_rows;
+  p.x = x;
+  p.idx = indices;
+  p.out = out;
+  p.n_out = (int)k;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_GATHER, EPI_PLAIN>(p, (cudaStream_t)stream);
+}
+
+extern "C" int dip_gather_up_h(const int8_t* up_qw, const dip_bf16* up_sc, int64_t n_rows,
+                               const dip_bf16* x, const dip_bf16* g, const int32_t* idx,
+                               int64_t k, int64_t in_features, dip_bf16* h,
+                               dip_stream_t stream) {
+  if (k < 0 || k > INT32_MAX || n_rows < 0 || !gemv_shape_ok(in_features)) return DIP_ERR_ARG;
+  if (k == 0) return DIP_OK;
+  if (!up_qw || !up_sc || !x || !g || !idx || !h || n_rows == 0 || !aligned16(up_qw) ||
+      !aligned16(x))
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(up_qw);
+  p.sc0 = up_sc;
+  p.n0 = n_rows;
+  p.x = x;
+  p.idx = idx;
+  p.g = g;
+  p.gid = idx;
+  p.out = h;
+  p.n_out = (int)k;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_GATHER, EPI_H>(p, (cudaStream_t)stream);
+}
+
+extern "C" int dip_ca_fused_gemv(const int8_t* res_qw, const dip_bf16* res_sc, int64_t n_res,
+                                 const int8_t* str_qw, const dip_bf16* str_sc, int64_t n_str,
+                                 const dip_bf16* x, const int32_t* src, const int32_t* row,
+                                 int64_t k, int64_t in_features, dip_bf16* out,
+                                 dip_stream_t stream) {
+  if (k < 0 || k > INT32_MAX || n_res < 0 || n_str < 0 || !gemv_shape_ok(in_features))
+    return DIP_ERR_ARG;
+  if (k == 0) return DIP_OK;
+  if (!res_qw || !res_sc || !str_qw || !str_sc || !x || !src || !row || !out ||
+      !aligned16(res_qw) || !aligned16(str_qw) || !aligned16(x) || n_res + n_str == 0)
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(res_qw);
+  p.sc0 = res_sc;
+  p.n0 = n_res;
+  p.qw1 = reinterpret_cast<const uint8_t*>(str_qw);
+  p.sc1 = str_sc;
+  p.n1 = n_str;
+  p.x = x;
+  p.src = src;
+  p.row = row;
+  p.out = out;
+  p.n_out = (int)k;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_SRCROW, EPI_PLAIN>(p, (cudaStream_t)stream);
+}
+
+extern "C" int dip_srcrow_up_h(const int8_t* res_qw, const dip_bf16* res_sc, int64_t n_res,
+                               const int8_t* full_qw, const dip_bf16* full_sc, int64_t n_full,
+                               const dip_bf16* x, const dip_bf16* g,
+                               const int32_t* combined_ids, const int32_t* src,
+                               const int32_t* row, int64_t k, int64_t in_features, dip_bf16* h,
+                               dip_stream_t stream) {
+  if (k < 0 || k > INT32_MAX || n_res < 0 || n_full <= 0 || !gemv_shape_ok(in_features))
+    return DIP_ERR_ARG;
+  if (k == 0) return DIP_OK;
+  if (!full_qw || !full_sc || !x || !g || !combined_ids || !src || !row || !h ||
+      !aligned16(full_qw) || !aligned16(x) || (n_res > 0 && (!res_qw || !res_sc)))
+    return DIP_ERR_ARG;
+  if (n_res > 0 && !aligned16(res_qw)) return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(n_res > 0 ? res_qw : full_qw);
+  p.sc0 = n_res > 0 ? res_sc : full_sc;
+  p.n0 = n_res;
+  p.qw1 = reinterpret_cast<const uint8_t*>(full_qw);
+  p.sc1 = full_sc;
+  p.n1 = n_full;
+  p.x = x;
+  p.src = src;
+  p.row = row;
+  p.g = g;
+  p.gid = combined_ids;
+  p.out = h;
+  p.n_out = (int)k;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_SRCROW, EPI_H>(p, (cudaStream_t)stream);
+}

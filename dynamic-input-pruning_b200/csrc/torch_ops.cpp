@@ -1,0 +1,415 @@
+// torch_ops.cpp — thin torch extension over the C ABI (include/dip_b200.h).
+//
+// Registers the reference's five operator schemas unchanged, so code written
+// against the reference keeps calling torch.ops.<ns>.<op>:
+//   int4_ops::int4_gemv               kernels/int4_gemv/int4_gemv.cu:110-115
+//   topk_ops::topk_select             kernels/topk_select/topk_select.cu:166-171
+//   int4_gather_ops::int4_gather_gemv kernels/int4_gather/int4_gather_gemv.cu:110-115
+//   int4_down_ops::int4_gather_down   kernels/int4_down/int4_gather_down.cu:97-102
+//   ca_fused_ops::ca_fused_gemv       kernels/ca_fused/ca_fused_gemv.cu:107-112
+// plus the fused B200 operators of namespace dip_b200.  Unlike the reference
+// wrappers, every input is checked (device, dtype, shape, contiguity) and
+// every launch goes to torch's current stream.  Only the CUDA dispatch key is
+// implemented: there is no CPU kernel to fall back to.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <ATen/ATen.h>
+#include <torch/library.h>
+
+#include "../../include/dip_b200.h"
+
+namespace {
+
+using at::Tensor;
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == DIP_OK, what, " failed: ", dip_status_string(st),
+              st == DIP_ERR_CUDA ? std::string(" (") + dip_last_cuda_error() + ")" : "");
+}
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+void check_dtype(const Tensor& t, c10::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.scalar_type() == dt, name, " must be ", dt, ", got ", t.scalar_type());
+}
+void check_packed(const Tensor& qw, const Tensor& sc, const char* name) {
+  check_cuda(qw, name);
+  check_cuda(sc, name);
+  TORCH_CHECK(qw.dim() == 2 && sc.dim() == 2, name, ": qweight/scales must be 2-D");
+  TORCH_CHECK(qw.scalar_type() == at::kChar || qw.scalar_type() == at::kByte, name,
+              ": qweight must be int8");
+  check_dtype(sc, at::kBFloat16, name);
+  TORCH_CHECK(qw.size(0) == sc.size(0) && qw.size(1) * 2 == sc.size(1) * 128, name,
+              ": qweight [rows, in/2] and scales [rows, in/128] disagree");
+}
+Tensor idx32(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kInt || t.scalar_type() == at::kLong, name,
+              " must be int32 or int64");
+  return t.to(at::kInt).contiguous();
+}
+dip_stream_t cur_stream() {
+  return reinterpret_cast<dip_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+const int8_t* i8(const Tensor& t) { return reinterpret_cast<const int8_t*>(t.data_ptr()); }
+const dip_bf16* bf(const Tensor& t) { return reinterpret_cast<const dip_bf16*>(t.data_ptr()); }
+dip_bf16* bfm(Tensor& t) { return reinterpret_cast<dip_bf16*>(t.data_ptr()); }
+Tensor bf16_empty(int64_t n, const Tensor& like) {
+  return at::empty({n}, like.options().dtype(at::kBFloat16));
+}
+
+// ---------------- reference schemas ----------------
+Tensor int4_gemv(const Tensor& qweight, const Tensor& scales, const Tensor& x_in) {
+  check_packed(qweight, scales, "int4_gemv");
+  c10::cuda::CUDAGuard guard(qweight.device());
+  Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_dtype(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.numel() == qweight.size(1) * 2, "int4_gemv: x has ", x.numel(),
+              " elements, expected ", qweight.size(1) * 2);
+  Tensor out = bf16_empty(qweight.size(0), x);
+  check_status(dip_int4_gemv(i8(qweight), bf(scales), bf(x), bfm(out), qweight.size(0),
+                             qweight.size(1) * 2, 0, cur_stream()),
+               "int4_gemv");
+  return out;
+}
+
+Tensor topk_select(const Tensor& s_in, int64_t k) {
+  Tensor s = s_in.contiguous();
+  check_cuda(s, "s");
+  check_dtype(s, at::kBFloat16, "s");
+  c10::cuda::CUDAGuard guard(s.device());
+  TORCH_CHECK(k >= 0, "topk_select: k must be >= 0");
+  Tensor idx = at::empty({k}, s.options().dtype(at::kInt));
+  if (k == 0) return idx;
+  check_status(dip_topk_select(bf(s), s.numel(), k, idx.data_ptr<int32_t>(), cur_stream()),
+               "topk_select");
+  return idx;
+}
+
+Tensor int4_gather_gemv(const Tensor& qweight, const Tensor& scales, const Tensor& x_in,
+                        const Tensor& indices_in) {
+  check_packed(qweight, scales, "int4_gather_gemv");
+  c10::cuda::CUDAGuard guard(qweight.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.numel() == qweight.size(1) * 2, "int4_gather_gemv: x/qweight mismatch");
+  Tensor ind = idx32(indices_in, "indices");
+  Tensor out = bf16_empty(ind.numel(), x);
+  check_status(dip_int4_gather_gemv(i8(qweight), bf(scales), qweight.size(0), bf(x),
+                                    ind.data_ptr<int32_t>(), ind.numel(), qweight.size(1) * 2,
+                                    bfm(out), cur_stream()),
+               "int4_gather_gemv");
+  return out;
+}
+
+Tensor int4_gather_down(const Tensor& down_t_sel, const Tensor& scales, const Tensor& h_in) {
+  check_packed(down_t_sel, scales, "int4_gather_down");
+  c10::cuda::CUDAGuard guard(down_t_sel.device());
+  Tensor h = h_in.contiguous();
+  check_dtype(h, at::kBFloat16, "h_sel");
+  TORCH_CHECK(h.numel() == down_t_sel.size(0), "int4_gather_down: h_sel has ", h.numel(),
+              " elements, down_t_sel has ", down_t_sel.size(0), " rows");
+  const int64_t out_f = down_t_sel.size(1) * 2;
+  Tensor y = bf16_empty(out_f, h);
+  Tensor ws = at::empty({(int64_t)dip_gather_down_workspace_bytes(out_f)},
+                        h.options().dtype(at::kByte));
+  check_status(dip_int4_gather_down(i8(down_t_sel), bf(scales), down_t_sel.size(0), bf(h),
+                                    nullptr, h.numel(), out_f, ws.data_ptr(), ws.numel(),
+                                    bfm(y), cur_stream()),
+               "int4_gather_down");
+  return y;
+}
+
+Tensor ca_fused_gemv(const Tensor& res_qw, const Tensor& res_sc, const Tensor& str_qw,
+                     const Tensor& str_sc, const Tensor& x_in, const Tensor& src_in,
+                     const Tensor& row_in) {
+  check_packed(res_qw, res_sc, "ca_fused_gemv(res)");
+  check_packed(str_qw, str_sc, "ca_fused_gemv(str)");
+  c10::cuda::CUDAGuard guard(res_qw.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  const int64_t in_f = x.numel();  // the reference takes in_features from x
+  TORCH_CHECK(res_qw.size(1) * 2 == in_f && str_qw.size(1) * 2 == in_f,
+              "ca_fused_gemv: x length does not match the packed rows");
+  Tensor src = idx32(src_in, "src"), row = idx32(row_in, "row");
+  TORCH_CHECK(src.numel() == row.numel(), "ca_fused_gemv: src/row length mismatch");
+  Tensor out = bf16_empty(src.numel(), x);
+  check_status(dip_ca_fused_gemv(i8(res_qw), bf(res_sc), res_qw.size(0), i8(str_qw), bf(str_sc),
+                                 str_qw.size(0), bf(x), src.data_ptr<int32_t>(),
+                                 row.data_ptr<int32_t>(), src.numel(), in_f, bfm(out),
+                                 cur_stream()),
+               "ca_fused_gemv");
+  return out;
+}
+
+// ---------------- B200 fused operators ----------------
+Tensor gate_silu(const Tensor& qweight, const Tensor& scales, const Tensor& x_in) {
+  check_packed(qweight, scales, "gate_silu");
+  c10::cuda::CUDAGuard guard(qweight.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.numel() == qweight.size(1) * 2, "gate_silu: x/qweight mismatch");
+  Tensor out = bf16_empty(qweight.size(0), x);
+  check_status(dip_int4_gemv(i8(qweight), bf(scales), bf(x), bfm(out), qweight.size(0),
+                             qweight.size(1) * 2, 1, cur_stream()),
+               "gate_silu");
+  return out;
+}
+
+Tensor topk_select_batched(const Tensor& s_in, int64_t k) {
+  Tensor s = s_in.contiguous();
+  check_cuda(s, "s");
+  check_dtype(s, at::kBFloat16, "s");
+  TORCH_CHECK(s.dim() == 2, "topk_select_batched: s must be [B, n]");
+  c10::cuda::CUDAGuard guard(s.device());
+  Tensor idx = at::empty({s.size(0), k}, s.options().dtype(at::kInt));
+  if (k == 0 || s.size(0) == 0) return idx;
+  check_status(dip_topk_select_batched(bf(s), s.size(0), s.size(1), s.size(1), k,
+                                       idx.data_ptr<int32_t>(), k, cur_stream()),
+               "topk_select_batched");
+  return idx;
+}
+
+Tensor gather_up_h(const Tensor& up_qw, const Tensor& up_sc, const Tensor& x_in,
+                   const Tensor& g_in, const Tensor& idx_in) {
+  check_packed(up_qw, up_sc, "gather_up_h");
+  c10::cuda::CUDAGuard guard(up_qw.device());
+  Tensor x = x_in.contiguous(), g = g_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  check_dtype(g, at::kBFloat16, "g");
+  TORCH_CHECK(x.numel() == up_qw.size(1) * 2, "gather_up_h: x/up_qw mismatch");
+  TORCH_CHECK(g.numel() == up_qw.size(0), "gather_up_h: g must have one value per row");
+  Tensor idx = idx32(idx_in, "idx");
+  Tensor h = bf16_empty(idx.numel(), x);
+  check_status(dip_gather_up_h(i8(up_qw), bf(up_sc), up_qw.size(0), bf(x), bf(g),
+                               idx.data_ptr<int32_t>(), idx.numel(), up_qw.size(1) * 2, bfm(h),
+                               cur_stream()),
+               "gather_up_h");
+  return h;
+}
+
+Tensor gather_down_idx(const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& h_in,
+                       const Tensor& idx_in) {
+  check_packed(dt_qw, dt_sc, "gather_down_idx");
+  c10::cuda::CUDAGuard guard(dt_qw.device());
+  Tensor h = h_in.contiguous();
+  check_dtype(h, at::kBFloat16, "h");
+  Tensor idx = idx32(idx_in, "idx");
+  TORCH_CHECK(h.numel() == idx.numel(), "gather_down_idx: h/idx length mismatch");
+  const int64_t out_f = dt_qw.size(1) * 2;
+  Tensor y = bf16_empty(out_f, h);
+  Tensor ws = at::empty({(int64_t)dip_gather_down_workspace_bytes(out_f)},
+                        h.options().dtype(at::kByte));
+  check_status(dip_int4_gather_down(i8(dt_qw), bf(dt_sc), dt_qw.size(0), bf(h),
+                                    idx.data_ptr<int32_t>(), idx.numel(), out_f, ws.data_ptr(),
+                                    ws.numel(), bfm(y), cur_stream()),
+               "gather_down_idx");
+  return y;
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> ca_split(const Tensor& idx_in,
+                                                    const Tensor& id2slot_in) {
+  Tensor idx = idx32(idx_in, "idx");
+  TORCH_CHECK(id2slot_in.is_cuda() && id2slot_in.scalar_type() == at::kLong,
+              "ca_split: id2slot must be a CUDA int64 tensor");
+  Tensor id2slot = id2slot_in.contiguous();
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int64_t k = idx.numel();
+  auto iopt = idx.options().dtype(at::kInt);
+  Tensor comb = at::empty({k}, iopt), src = at::empty({k}, iopt), row = at::empty({k}, iopt);
+  Tensor nhit = at::empty({1}, iopt);
+  check_status(dip_ca_split(idx.data_ptr<int32_t>(), k, id2slot.data_ptr<int64_t>(),
+                            id2slot.numel(), comb.data_ptr<int32_t>(), src.data_ptr<int32_t>(),
+                            row.data_ptr<int32_t>(), nhit.data_ptr<int32_t>(), cur_stream()),
+               "ca_split");
+  return {comb, src, row, nhit};
+}
+
+Tensor srcrow_up_h(const Tensor& res_qw, const Tensor& res_sc, const Tensor& full_qw,
+                   const Tensor& full_sc, const Tensor& x_in, const Tensor& g_in,
+                   const Tensor& comb_in, const Tensor& src_in, const Tensor& row_in) {
+  check_packed(full_qw, full_sc, "srcrow_up_h(full)");
+  check_packed(res_qw, res_sc, "srcrow_up_h(res)");
+  c10::cuda::CUDAGuard guard(full_qw.device());
+  Tensor x = x_in.contiguous(), g = g_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  check_dtype(g, at::kBFloat16, "g");
+  TORCH_CHECK(x.numel() == full_qw.size(1) * 2 && res_qw.size(1) == full_qw.size(1),
+              "srcrow_up_h: shape mismatch");
+  Tensor comb = idx32(comb_in, "combined_ids"), src = idx32(src_in, "src"),
+         row = idx32(row_in, "row");
+  Tensor h = bf16_empty(src.numel(), x);
+  check_status(dip_srcrow_up_h(i8(res_qw), bf(res_sc), res_qw.size(0), i8(full_qw), bf(full_sc),
+                               full_qw.size(0), bf(x), bf(g), comb.data_ptr<int32_t>(),
+                               src.data_ptr<int32_t>(), row.data_ptr<int32_t>(), src.numel(),
+                               full_qw.size(1) * 2, bfm(h), cur_stream()),
+               "srcrow_up_h");
+  return h;
+}
+
+Tensor srcrow_down(const Tensor& res_dt, const Tensor& res_sc, const Tensor& full_dt,
+                   const Tensor& full_sc, const Tensor& h_in, const Tensor& src_in,
+                   const Tensor& row_in) {
+  check_packed(full_dt, full_sc, "srcrow_down(full)");
+  check_packed(res_dt, res_sc, "srcrow_down(res)");
+  c10::cuda::CUDAGuard guard(full_dt.device());
+  Tensor h = h_in.contiguous();
+  check_dtype(h, at::kBFloat16, "h");
+  Tensor src = idx32(src_in, "src"), row = idx32(row_in, "row");
+  const int64_t out_f = full_dt.size(1) * 2;
+  Tensor y = bf16_empty(out_f, h);
+  Tensor ws = at::empty({(int64_t)dip_gather_down_workspace_bytes(out_f)},
+                        h.options().dtype(at::kByte));
+  check_status(dip_srcrow_down(i8(res_dt), bf(res_sc), res_dt.size(0), i8(full_dt), bf(full_sc),
+                               full_dt.size(0), bf(h), src.data_ptr<int32_t>(),
+                               row.data_ptr<int32_t>(), src.numel(), out_f, ws.data_ptr(),
+                               ws.numel(), bfm(y), cur_stream()),
+               "srcrow_down");
+  return y;
+}
+
+std::tuple<Tensor, Tensor, Tensor> mlp_decode(const Tensor& gate_qw, const Tensor& gate_sc,
+                                              const Tensor& up_qw, const Tensor& up_sc,
+                                              const Tensor& dt_qw, const Tensor& dt_sc,
+                                              const Tensor& x_in, int64_t k) {
+  check_packed(gate_qw, gate_sc, "mlp_decode(gate)");
+  check_packed(up_qw, up_sc, "mlp_decode(up)");
+  check_packed(dt_qw, dt_sc, "mlp_decode(down_t)");
+  c10::cuda::CUDAGuard guard(gate_qw.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  const int64_t hidden = gate_qw.size(1) * 2, inter = gate_qw.size(0);
+  TORCH_CHECK(x.numel() == hidden && up_qw.sizes() == gate_qw.sizes() &&
+                  dt_qw.size(0) == inter && dt_qw.size(1) * 2 == hidden,
+              "mlp_decode: shape mismatch");
+  dip_layer_t L = {i8(gate_qw), bf(gate_sc), i8(up_qw), bf(up_sc), i8(dt_qw), bf(dt_sc),
+                   hidden, inter};
+  Tensor y = bf16_empty(hidden, x), g = bf16_empty(inter, x);
+  Tensor idx = at::empty({k}, x.options().dtype(at::kInt));
+  const size_t wsb = dip_mlp_workspace_bytes(hidden, inter, k);
+  Tensor ws = at::empty({(int64_t)wsb}, x.options().dtype(at::kByte));
+  check_status(dip_mlp_decode(&L, bf(x), k, ws.data_ptr(), wsb, bfm(y), bfm(g),
+                              idx.data_ptr<int32_t>(), cur_stream()),
+               "mlp_decode");
+  return {y, g, idx};
+}
+
+std::tuple<Tensor, Tensor> quantize_int4(const Tensor& w_in) {
+  Tensor w = w_in.contiguous();
+  check_cuda(w, "w");
+  check_dtype(w, at::kBFloat16, "w");
+  TORCH_CHECK(w.dim() == 2 && w.size(1) % 128 == 0, "quantize_int4: w must be [out, in%128==0]");
+  c10::cuda::CUDAGuard guard(w.device());
+  Tensor qw = at::empty({w.size(0), w.size(1) / 2}, w.options().dtype(at::kChar));
+  Tensor sc = at::empty({w.size(0), w.size(1) / 128}, w.options());
+  check_status(dip_quantize_int4_g128(bf(w), w.size(0), w.size(1),
+                                      reinterpret_cast<int8_t*>(qw.data_ptr()), bfm(sc),
+                                      cur_stream()),
+               "quantize_int4");
+  return {qw, sc};
+}
+
+Tensor dequantize_int4(const Tensor& qw, const Tensor& sc) {
+  check_packed(qw, sc, "dequantize_int4");
+  c10::cuda::CUDAGuard guard(qw.device());
+  Tensor w = at::empty({qw.size(0), qw.size(1) * 2}, sc.options());
+  check_status(dip_dequantize_int4_g128(i8(qw), bf(sc), qw.size(0), qw.size(1) * 2, bfm(w),
+                                        cur_stream()),
+               "dequantize_int4");
+  return w;
+}
+
+std::tuple<Tensor, Tensor> transpose_down_int4(const Tensor& dqw, const Tensor& dsc) {
+  check_packed(dqw, dsc, "transpose_down_int4");
+  c10::cuda::CUDAGuard guard(dqw.device());
+  const int64_t out_f = dqw.size(0), inter = dqw.size(1) * 2;
+  TORCH_CHECK(out_f % 128 == 0, "transpose_down_int4: out_features must be a multiple of 128");
+  Tensor tq = at::empty({inter, out_f / 2}, dqw.options().dtype(at::kChar));
+  Tensor ts = at::empty({inter, out_f / 128}, dsc.options());
+  check_status(dip_transpose_down_int4(i8(dqw), bf(dsc), out_f, inter,
+                                       reinterpret_cast<int8_t*>(tq.data_ptr()), bfm(ts),
+                                       cur_stream()),
+               "transpose_down_int4");
+  return {tq, ts};
+}
+
+Tensor residual_rmsnorm(const Tensor& y_in, const Tensor& r_in, double eps) {
+  Tensor y = y_in.contiguous(), r = r_in.contiguous();
+  check_cuda(y, "y");
+  check_cuda(r, "r");
+  check_dtype(y, at::kBFloat16, "y");
+  check_dtype(r, at::kBFloat16, "r");
+  TORCH_CHECK(y.numel() == r.numel(), "residual_rmsnorm: y/r size mismatch");
+  c10::cuda::CUDAGuard guard(y.device());
+  Tensor out = at::empty_like(y);
+  check_status(dip_residual_rmsnorm(bf(y), bf(r), y.numel(), (float)eps, bfm(out), cur_stream()),
+               "residual_rmsnorm");
+  return out;
+}
+
+int64_t op_set_pdl(int64_t enable) { return dip_set_pdl((int)enable); }
+
+}  // namespace
+
+TORCH_LIBRARY(int4_ops, m) { m.def("int4_gemv(Tensor qweight, Tensor scales, Tensor x) -> Tensor"); }
+TORCH_LIBRARY_IMPL(int4_ops, CUDA, m) { m.impl("int4_gemv", &int4_gemv); }
+
+TORCH_LIBRARY(topk_ops, m) { m.def("topk_select(Tensor s, int k) -> Tensor"); }
+TORCH_LIBRARY_IMPL(topk_ops, CUDA, m) { m.impl("topk_select", &topk_select); }
+
+TORCH_LIBRARY(int4_gather_ops, m) {
+  m.def("int4_gather_gemv(Tensor qweight, Tensor scales, Tensor x, Tensor indices) -> Tensor");
+}
+TORCH_LIBRARY_IMPL(int4_gather_ops, CUDA, m) { m.impl("int4_gather_gemv", &int4_gather_gemv); }
+
+TORCH_LIBRARY(int4_down_ops, m) {
+  m.def("int4_gather_down(Tensor down_t_sel, Tensor scales, Tensor h_sel) -> Tensor");
+}
+TORCH_LIBRARY_IMPL(int4_down_ops, CUDA, m) { m.impl("int4_gather_down", &int4_gather_down); }
+
+TORCH_LIBRARY(ca_fused_ops, m) {
+  m.def(
+      "ca_fused_gemv(Tensor res_qw, Tensor res_sc, Tensor str_qw, Tensor str_sc, Tensor x, "
+      "Tensor src, Tensor row) -> Tensor");
+}
+TORCH_LIBRARY_IMPL(ca_fused_ops, CUDA, m) { m.impl("ca_fused_gemv", &ca_fused_gemv); }
+
+TORCH_LIBRARY(dip_b200, m) {
+  m.def("gate_silu(Tensor qweight, Tensor scales, Tensor x) -> Tensor");
+  m.def("topk_select_batched(Tensor s, int k) -> Tensor");
+  m.def("gather_up_h(Tensor up_qw, Tensor up_sc, Tensor x, Tensor g, Tensor idx) -> Tensor");
+  m.def("gather_down_idx(Tensor down_t_qw, Tensor down_t_sc, Tensor h, Tensor idx) -> Tensor");
+  m.def("ca_split(Tensor idx, Tensor id2slot) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def(
+      "srcrow_up_h(Tensor res_qw, Tensor res_sc, Tensor full_qw, Tensor full_sc, Tensor x, "
+      "Tensor g, Tensor combined_ids, Tensor src, Tensor row) -> Tensor");
+  m.def(
+      "srcrow_down(Tensor res_dt, Tensor res_sc, Tensor full_dt, Tensor full_sc, Tensor h, "
+      "Tensor src, Tensor row) -> Tensor");
+  m.def(
+      "mlp_decode(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, Tensor down_t_qw, "
+      "Tensor down_t_sc, Tensor x, int k) -> (Tensor, Tensor, Tensor)");
+  m.def("quantize_int4(Tensor w) -> (Tensor, Tensor)");
+  m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
+  m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
+  m.def("residual_rmsnorm(Tensor y, Tensor r, float eps) -> Tensor");
+  m.def("set_pdl(int enable) -> int");
+}
+TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
+  m.impl("gate_silu", &gate_silu);
+  m.impl("topk_select_batched", &topk_select_batched);
+  m.impl("gather_up_h", &gather_up_h);
+  m.impl("gather_down_idx", &gather_down_idx);
+  m.impl("ca_split", &ca_split);
+  m.impl("srcrow_up_h", &srcrow_up_h);
+  m.impl("srcrow_down", &srcrow_down);
+  m.impl("mlp_decode", &mlp_decode);
+  m.impl("quantize_int4", &quantize_int4);
+  m.impl("dequantize_int4", &dequantize_int4);
+  m.impl("transpose_down_int4", &transpose_down_int4);
+  m.impl("residual_rmsnorm", &residual_rmsnorm);
+}
+TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) { m.impl("set_pdl", &op_set_pdl); }

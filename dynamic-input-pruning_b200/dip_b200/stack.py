@@ -1,0 +1,158 @@
+"""Synthetic Qwen3-32B-shaped DIP decode stack (BASELINE configs 1 and 2).
+
+Per layer the input is RMSNorm(prev_y + r) with unit weight, r an N(0,1) bf16
+residual; the first layer's input is an N(0,1) token.  Weights are bf16
+N(0, 0.02) generated on the GPU from per-layer seeds, quantised int4 g128
+with the sm_100a quantiser (bit exact with scripts/quantize.py) and down is
+transposed with _transpose_down_to_int4's rule.  The whole stack (64 x ~203
+MB) stays resident in HBM.
+
+`DipStack.decode(x0, resid)` is the public call: one token through every
+layer, replayed from a CUDA graph captured on first use for the given
+buffers' shapes.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import load_ops
+
+load_ops()
+
+RMS_EPS = 1e-6
+
+
+@dataclass
+class StackConfig:
+    n_layers: int = 64
+    hidden: int = 5120
+    inter: int = 25600
+    keep_ratio: float = 0.6
+    cache_frac: float = 0.3
+    seed: int = 0
+    std: float = 0.02
+    gate_lognormal: bool = False  # config 2: per-channel LogNormal(0,1) gate row scale
+
+    @property
+    def k(self) -> int:
+        return max(1, int(round(self.inter * self.keep_ratio)))
+
+    @property
+    def cache_n(self) -> int:
+        return int(round(self.inter * self.cache_frac))
+
+
+def make_layer(cfg: StackConfig, layer: int, device) -> dict:
+    """One layer's packed weights, generated and quantised on `device`."""
+    gen = torch.Generator(device=device).manual_seed(cfg.seed * 100003 + layer)
+    H, I = cfg.hidden, cfg.inter
+    q = torch.ops.dip_b200.quantize_int4
+    wg = torch.randn(I, H, generator=gen, device=device) * cfg.std
+    if cfg.gate_lognormal:
+        scale = torch.exp(torch.randn(I, 1, generator=gen, device=device))
+        wg = wg * scale
+    gq, gs = q(wg.to(torch.bfloat16))
+    del wg
+    wu = (torch.randn(I, H, generator=gen, device=device) * cfg.std).to(torch.bfloat16)
+    uq, us = q(wu)
+    del wu
+    wd = (torch.randn(H, I, generator=gen, device=device) * cfg.std).to(torch.bfloat16)
+    dq, ds = q(wd)
+    del wd
+    tq, ts = torch.ops.dip_b200.transpose_down_int4(dq, ds)
+    return {"gate_qw": gq, "gate_sc": gs, "up_qw": uq, "up_sc": us, "down_t_qw": tq,
+            "down_t_sc": ts}
+
+
+def layer_weight_bytes(cfg: StackConfig) -> dict:
+    """Algorithmic HBM bytes one decode step of one layer must read."""
+    row = cfg.hidden // 2 + 2 * (cfg.hidden // 128)
+    return {"gate": cfg.inter * row, "up": cfg.k * row, "down": cfg.k * row,
+            "total": (cfg.inter + 2 * cfg.k) * row}
+
+
+class DipStack:
+    """A stack of resident DIP MLP layers with the synthetic inter-layer step."""
+
+    def __init__(self, cfg: StackConfig, device="cuda:0", layers: list | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.layers = layers if layers is not None else [
+            make_layer(cfg, l, self.device) for l in range(cfg.n_layers)]
+        self._graph = None
+        self._static_in = None
+        self._static_out = None
+        # Last token's per-layer selections (filled by decode_eager).
+        self.last_idx = None
+
+    # -- one token, eager -------------------------------------------------
+    def step(self, x0: torch.Tensor, resid: torch.Tensor, record: bool = False) -> torch.Tensor:
+        """x0 [hidden] bf16, resid [n_layers, hidden] bf16 -> last layer's y."""
+        x = x0
+        k = self.cfg.k
+        idxs = []
+        y = None
+        for l, L in enumerate(self.layers):
+            if l > 0:
+                x = torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
+            y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"], L["up_qw"],
+                                                      L["up_sc"], L["down_t_qw"],
+                                                      L["down_t_sc"], x, k)
+            if record:
+                idxs.append(idx)
+        if record:
+            self.last_idx = idxs
+        return y
+
+    # -- one token, CUDA graph --------------------------------------------
+    def capture(self) -> None:
+        H, n = self.cfg.hidden, self.cfg.n_layers
+        self._static_in = (torch.zeros(H, dtype=torch.bfloat16, device=self.device),
+                           torch.zeros(n, H, dtype=torch.bfloat16, device=self.device))
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm the allocator and kernels before capture
+                self.step(*self._static_in)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._static_out = self.step(*self._static_in)
+        self._graph = g
+
+    def replay(self) -> torch.Tensor:
+        self._graph.replay()
+        return self._static_out
+
+    def decode(self, x0: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+        """Public call: one decode token through every layer.  Inputs may live
+        on the host (copied in) or the device; returns y on the inputs' device."""
+        if self._graph is None:
+            self.capture()
+        xi, ri = self._static_in
+        xi.copy_(x0, non_blocking=True)
+        ri.copy_(resid, non_blocking=True)
+        out = self.replay()
+        if x0.device.type == "cpu":
+            res = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            res.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            return res
+        return out
+
+
+def make_stack(cfg: StackConfig, device="cuda:0") -> DipStack:
+    return DipStack(cfg, device)
+
+
+def token_inputs(cfg: StackConfig, n_tokens: int, seed: int, device="cpu"):
+    """Seeded N(0,1) bf16 first-layer inputs [T, H] and residuals [T, L, H]."""
+    gen = torch.Generator().manual_seed(seed)
+    x0 = torch.randn(n_tokens, cfg.hidden, generator=gen).to(torch.bfloat16)
+    r = torch.randn(n_tokens, cfg.n_layers, cfg.hidden, generator=gen).to(torch.bfloat16)
+    if device != "cpu":
+        x0, r = x0.to(device), r.to(device)
+    return x0, r

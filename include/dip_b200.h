@@ -1,0 +1,187 @@
+/*
+ * dip_b200.h — C ABI of the B200 (sm_100a) Dynamic Input Pruning MLP kernels.
+ *
+ * Every entry point takes raw DEVICE pointers, element counts and a CUDA
+ * stream, launches asynchronously on that stream and returns a status code
+ * (DIP_OK = 0).  Nothing here allocates device memory: outputs and scratch
+ * ("workspace") are provided by the caller, sized with the *_workspace_bytes
+ * helpers.  bf16 tensors are passed as arrays of 16-bit patterns (dip_bf16).
+ *
+ * Weight format (unchanged from the reference, scripts/quantize.py:32-64):
+ *   qweight int8 [rows, in/2], two's complement nibbles, low nibble = even col
+ *   scales  bf16 [rows, in/128], w = q * s
+ * down_proj is used in the transposed layout produced by
+ * dip_stream_predispatch.py:100-120 (_transpose_down_to_int4):
+ *   down_t  int8 [inter, hidden/2], scales bf16 [inter, hidden/128].
+ *
+ * Each declaration names the reference interface it replaces (file:line in
+ * the reference project).
+ */
+#ifndef DIP_B200_H_
+#define DIP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DIP_API __attribute__((visibility("default")))
+#else
+#define DIP_API
+#endif
+
+typedef struct CUstream_st* dip_stream_t; /* == cudaStream_t */
+typedef uint16_t dip_bf16;                /* raw bfloat16 bits */
+
+#define DIP_OK 0
+#define DIP_ERR_ARG 1         /* null pointer, bad size or misaligned pointer */
+#define DIP_ERR_CUDA 2        /* a CUDA launch / runtime error */
+#define DIP_ERR_WORKSPACE 3   /* caller workspace smaller than required */
+#define DIP_ERR_UNSUPPORTED 4 /* shape outside what the kernels handle */
+
+/* Library version (major*10000 + minor*100 + patch). */
+DIP_API int dip_version(void);
+/* Human readable text of a status code; never NULL. */
+DIP_API const char* dip_status_string(int status);
+/* Last CUDA error text seen by the library on this thread (or ""). */
+DIP_API const char* dip_last_cuda_error(void);
+/* Enable (1) / disable (0) programmatic dependent launch between the kernels
+ * of one call chain.  Default 1.  Returns the previous setting. */
+DIP_API int dip_set_pdl(int enable);
+
+/* ---- a5/a6: int4 GEMV, optionally fused with SiLU --------------------------
+ * out[r] = bf16(sum_c q[r,c]*s[r,c/128]*x[c]); with apply_silu != 0 the result
+ * is then g = bf16(silu(out)).  Replaces int4_ops::int4_gemv
+ * (kernels/int4_gemv/int4_gemv.cu:89-115) and the separate F.silu of
+ * dip_stream_predispatch.py:182.  in_features % 128 == 0. */
+DIP_API int dip_int4_gemv(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
+                  dip_bf16* out, int64_t rows, int64_t in_features, int apply_silu,
+                  dip_stream_t stream);
+
+/* ---- a7: top-k of |s| -------------------------------------------------------
+ * Exactly the selection of topk_ops::topk_select
+ * (kernels/topk_select/topk_select.cu:134-164): 25-step fp32 bisection on
+ * [0, max|s|], then indices with |s| > hi in ascending order followed by
+ * lo < |s| <= hi in ascending order, truncated to k; unfilled slots are 0.
+ * One launch, no host synchronisation.  1 <= n <= 98304, 0 <= k. */
+DIP_API int dip_topk_select(const dip_bf16* s, int64_t n, int64_t k, int32_t* idx,
+                    dip_stream_t stream);
+/* Per-token variant for batched decode (one CTA per row of s): row b of s
+ * starts at s + b*s_stride, its k indices at idx + b*idx_stride.  The
+ * reference decode path is batch-1 only (dip_stream_predispatch.py:170,182);
+ * each row gets exactly the selection of dip_topk_select. */
+DIP_API int dip_topk_select_batched(const dip_bf16* s, int64_t batch, int64_t n, int64_t s_stride,
+                            int64_t k, int32_t* idx, int64_t idx_stride, dip_stream_t stream);
+
+/* ---- a8: gathered int4 GEMV --------------------------------------------------
+ * out[j] = bf16(dot(dequant(W[indices[j]]), x)), j < k.  Replaces
+ * int4_gather_ops::int4_gather_gemv (kernels/int4_gather/int4_gather_gemv.cu:
+ * 87-115).  n_rows bounds the index range (out-of-range indices read row 0
+ * and set the result to 0). */
+DIP_API int dip_int4_gather_gemv(const int8_t* qweight, const dip_bf16* scales, int64_t n_rows,
+                         const dip_bf16* x, const int32_t* indices, int64_t k,
+                         int64_t in_features, dip_bf16* out, dip_stream_t stream);
+
+/* ---- a8+a9: gathered up GEMV with the g*u product folded in --------------------
+ * h[j] = bf16(g[idx[j]] * bf16(dot(W_up[idx[j]], x))).  Replaces the up call
+ * and the `h_sel = (g[idx] * up_sel).to(bf16)` line of
+ * dip_stream_predispatch.py:199-201. */
+DIP_API int dip_gather_up_h(const int8_t* up_qw, const dip_bf16* up_sc, int64_t n_rows,
+                    const dip_bf16* x, const dip_bf16* g, const int32_t* idx, int64_t k,
+                    int64_t in_features, dip_bf16* h, dip_stream_t stream);
+
+/* ---- a10: gathered transposed down projection -------------------------------
+ * y[o] = bf16(sum_j h[j] * q(down_t[r_j, o]) * s(down_t[r_j, o/128])) with
+ * r_j = idx[j] (or r_j = j when idx == NULL, the reference's staging-buffer
+ * layout).  Replaces int4_down_ops::int4_gather_down
+ * (kernels/int4_down/int4_gather_down.cu:77-102).  The cross-CTA sum is
+ * deterministic (fixed order, no float atomics). */
+DIP_API size_t dip_gather_down_workspace_bytes(int64_t out_features);
+DIP_API int dip_int4_gather_down(const int8_t* down_t, const dip_bf16* scales, int64_t n_rows,
+                         const dip_bf16* h, const int32_t* idx, int64_t k,
+                         int64_t out_features, void* workspace, size_t workspace_bytes,
+                         dip_bf16* y, dip_stream_t stream);
+
+/* ---- a13: dual-source gathered GEMV (cache-aware up) ---------------------------
+ * out[j] = dot(dequant(src[j]==0 ? res[row[j]] : str[row[j]]), x).  Replaces
+ * ca_fused_ops::ca_fused_gemv (kernels/ca_fused/ca_fused_gemv.cu:87-112);
+ * in_features is the length of x, as in the reference wrapper. */
+DIP_API int dip_ca_fused_gemv(const int8_t* res_qw, const dip_bf16* res_sc, int64_t n_res,
+                      const int8_t* str_qw, const dip_bf16* str_sc, int64_t n_str,
+                      const dip_bf16* x, const int32_t* src, const int32_t* row, int64_t k,
+                      int64_t in_features, dip_bf16* out, dip_stream_t stream);
+
+/* ---- a12: cache hit/miss split -------------------------------------------------
+ * For slots = id2slot[idx]: hits (slot >= 0) in idx order, then misses in idx
+ * order, as dip_ca.py:137-142 and :164-171.  Writes combined_ids[k], src[k]
+ * (0 = resident cache, 1 = full weights), row[k] (cache slot for a hit, the
+ * channel id for a miss) and n_hit[0].  One launch, no host synchronisation. */
+DIP_API int dip_ca_split(const int32_t* idx, int64_t k, const int64_t* id2slot, int64_t n_channels,
+                 int32_t* combined_ids, int32_t* src, int32_t* row, int32_t* n_hit,
+                 dip_stream_t stream);
+
+/* ---- a12/a13 fused: cache-aware up with h, and down, over (src,row) tables ----
+ * Source 0 = resident cache rows, source 1 = full resident rows. */
+DIP_API int dip_srcrow_up_h(const int8_t* res_qw, const dip_bf16* res_sc, int64_t n_res,
+                    const int8_t* full_qw, const dip_bf16* full_sc, int64_t n_full,
+                    const dip_bf16* x, const dip_bf16* g, const int32_t* combined_ids,
+                    const int32_t* src, const int32_t* row, int64_t k, int64_t in_features,
+                    dip_bf16* h, dip_stream_t stream);
+DIP_API int dip_srcrow_down(const int8_t* res_dt, const dip_bf16* res_sc, int64_t n_res,
+                    const int8_t* full_dt, const dip_bf16* full_sc, int64_t n_full,
+                    const dip_bf16* h, const int32_t* src, const int32_t* row, int64_t k,
+                    int64_t out_features, void* workspace, size_t workspace_bytes,
+                    dip_bf16* y, dip_stream_t stream);
+
+/* ---- a11: one whole decode DIP MLP layer, batch 1 --------------------------------
+ * gate GEMV + SiLU -> top-k -> gathered up (h) -> gathered down, four launches
+ * chained with programmatic dependent launch, no host synchronisation.
+ * Replaces StreamingDIPMlp.forward (dip_stream_predispatch.py:176-204). */
+typedef struct dip_layer {
+  const int8_t* gate_qw;   /* [inter, hidden/2]   */
+  const dip_bf16* gate_sc; /* [inter, hidden/128] */
+  const int8_t* up_qw;     /* [inter, hidden/2]   */
+  const dip_bf16* up_sc;   /* [inter, hidden/128] */
+  const int8_t* down_t_qw; /* [inter, hidden/2]   */
+  const dip_bf16* down_t_sc; /* [inter, hidden/128] */
+  int64_t hidden;
+  int64_t inter;
+} dip_layer_t;
+
+DIP_API size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k);
+/* g_out (bf16[inter]) and idx_out (int32[k]) may be NULL; when given they
+ * receive the layer's gate activations and selected channels. */
+DIP_API int dip_mlp_decode(const dip_layer_t* layer, const dip_bf16* x, int64_t k, void* workspace,
+                   size_t workspace_bytes, dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
+                   dip_stream_t stream);
+
+/* ---- a1/a3: weight format ---------------------------------------------------------
+ * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit
+ * exact with scripts/quantize.py:32-64. */
+DIP_API int dip_quantize_int4_g128(const dip_bf16* w, int64_t rows, int64_t cols, int8_t* qweight,
+                           dip_bf16* scales, dip_stream_t stream);
+/* dequantize -> transpose -> requantise along the new rows, bit exact with
+ * dip_stream_predispatch.py:100-120.  down_qw [out_f, inter/2] ->
+ * down_t_qw [inter, out_f/2], down_t_sc [inter, out_f/128]. */
+DIP_API int dip_transpose_down_int4(const int8_t* down_qw, const dip_bf16* down_sc, int64_t out_f,
+                            int64_t inter, int8_t* down_t_qw, dip_bf16* down_t_sc,
+                            dip_stream_t stream);
+/* Unpack + scale: w[r,c] = bf16(q*s), bit exact with qlinear.py:52-64. */
+DIP_API int dip_dequantize_int4_g128(const int8_t* qweight, const dip_bf16* scales, int64_t rows,
+                             int64_t cols, dip_bf16* w, dip_stream_t stream);
+
+/* ---- inter-layer step of the synthetic decode stack ---------------------------
+ * x_next = bf16(v * rsqrt(mean(v^2) + eps)), v = y + r (RMSNorm with unit
+ * weight of a layer output plus a residual).  Not part of the reference's
+ * MLP; it defines the per-layer inputs of the 64-layer benchmark stack. */
+DIP_API int dip_residual_rmsnorm(const dip_bf16* y, const dip_bf16* r, int64_t n, float eps,
+                                 dip_bf16* out, dip_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIP_B200_H_ */
