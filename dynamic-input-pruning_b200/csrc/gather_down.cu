@@ -31,6 +31,7 @@ struct DownParams {
   const int32_t* src;     // SRCROW
   const int32_t* row;     // SRCROW
   float* partial;         // [gridDim.x, out]
+  const int32_t* count;   // optional device-side number of rows (<= k)
   int k;
   int out_features;
 };
@@ -90,15 +91,17 @@ gather_down_kernel(const DownParams p) {
   const int teams = blockDim.x / nch;
   const int team = threadIdx.x / nch;
   const int ch = threadIdx.x - team * nch;
-  // Rows [j0, j1) of this CTA (balanced split).
-  const int j0 = (int)((int64_t)p.k * blockIdx.x / gridDim.x);
-  const int j1 = (int)((int64_t)p.k * (blockIdx.x + 1) / gridDim.x);
-
   float2 acc[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.f, 0.f);
 
   pdl_wait();
+  int k = p.k;
+  if (p.count) k = min(k, *p.count);
+  // Rows [j0, j1) of this CTA (balanced split).
+  const int j0 = (int)((int64_t)k * blockIdx.x / gridDim.x);
+  const int j1 = (int)((int64_t)k * (blockIdx.x + 1) / gridDim.x);
+
   for (int jb = j0 + team; jb < j1; jb += teams * kDownUnroll) {
     uint4 wv[kDownUnroll];
     float hs[kDownUnroll];
@@ -264,5 +267,26 @@ extern "C" int dip_srcrow_down(const int8_t* res_dt, const dip_bf16* res_sc, int
   p.k = (int)k;
   p.out_features = (int)out_features;
   return launch_down<DROW_SRCROW>(p, y, nullptr, workspace, workspace_bytes,
+                                  (cudaStream_t)stream);
+}
+
+extern "C" int dip_gather_down_partial(const int8_t* down_t, const dip_bf16* scales,
+                                       int64_t n_rows, const dip_bf16* h, const int32_t* idx,
+                                       const int32_t* count, int64_t max_k, int64_t out_features,
+                                       void* workspace, size_t workspace_bytes, float* y_f32,
+                                       dip_stream_t stream) {
+  if (max_k <= 0 || max_k > INT32_MAX || n_rows <= 0 || !down_shape_ok(out_features))
+    return DIP_ERR_ARG;
+  if (!down_t || !scales || !h || !idx || !y_f32 || !al16(down_t)) return DIP_ERR_ARG;
+  DownParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(down_t);
+  p.sc0 = scales;
+  p.n0 = n_rows;
+  p.h = h;
+  p.idx = idx;
+  p.count = count;
+  p.k = (int)max_k;
+  p.out_features = (int)out_features;
+  return launch_down<DROW_GATHER>(p, nullptr, y_f32, workspace, workspace_bytes,
                                   (cudaStream_t)stream);
 }

@@ -45,6 +45,7 @@ struct GemvParams {
   const uint16_t* g;   // EPI_H: gate activations by channel id
   const int32_t* gid;  // EPI_H: channel id of output j
   uint16_t* out;       // [n_out]
+  const int32_t* count;  // optional device-side number of outputs (<= n_out)
   int n_out;
   int in_features;
 };
@@ -95,12 +96,16 @@ gemv_int4_kernel(const GemvParams p) {
   const int tq = lane & 3;   // fragment column quad
   const int tile0 = blockIdx.x * 16;
 
-  // Rows of this lane: tile0+gq and tile0+gq+8 (clamped for the last tile).
-  const int ja = min(tile0 + gq, p.n_out - 1);
-  const int jb = min(tile0 + gq + 8, p.n_out - 1);
-
-  // Row indices of gathered modes come from the previous kernel.
+  // Row indices of gathered modes (and a device-side count) come from the
+  // previous kernel.
   if (MODE != ROW_DENSE) pdl_wait();
+  int n_out = p.n_out;
+  if (p.count) n_out = min(n_out, *p.count);
+  if (tile0 >= n_out) return;
+  // Rows of this lane: tile0+gq and tile0+gq+8 (clamped for the last tile).
+  const int ja = min(tile0 + gq, n_out - 1);
+  const int jb = min(tile0 + gq + 8, n_out - 1);
+
   const uint8_t *qa, *qb;
   const uint16_t *sa_p, *sb_p;
   const bool oka = resolve_row<MODE>(p, ja, qa, sa_p);
@@ -197,7 +202,7 @@ gemv_int4_kernel(const GemvParams p) {
   __syncthreads();
   if (threadIdx.x < 16) {
     const int j = tile0 + threadIdx.x;
-    if (j < p.n_out) {
+    if (j < n_out) {
       float v = red[threadIdx.x];
 #pragma unroll
       for (int w = 1; w < kGemvWarps; ++w) v += red[w * 16 + threadIdx.x];
@@ -364,4 +369,28 @@ extern "C" int dip_srcrow_up_h(const int8_t* res_qw, const dip_bf16* res_sc, int
   p.n_out = (int)k;
   p.in_features = (int)in_features;
   return launch_gemv<ROW_SRCROW, EPI_H>(p, (cudaStream_t)stream);
+}
+
+extern "C" int dip_gather_up_h_count(const int8_t* up_qw, const dip_bf16* up_sc, int64_t n_rows,
+                                     const dip_bf16* x, const dip_bf16* g, const int32_t* idx,
+                                     const int32_t* count, int64_t max_k, int64_t in_features,
+                                     dip_bf16* h, dip_stream_t stream) {
+  if (max_k < 0 || max_k > INT32_MAX || n_rows <= 0 || !gemv_shape_ok(in_features))
+    return DIP_ERR_ARG;
+  if (max_k == 0) return DIP_OK;
+  if (!up_qw || !up_sc || !x || !g || !idx || !count || !h || !aligned16(up_qw) || !aligned16(x))
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(up_qw);
+  p.sc0 = up_sc;
+  p.n0 = n_rows;
+  p.x = x;
+  p.idx = idx;
+  p.g = g;
+  p.gid = idx;
+  p.out = h;
+  p.count = count;
+  p.n_out = (int)max_k;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_GATHER, EPI_H>(p, (cudaStream_t)stream);
 }

@@ -87,39 +87,81 @@ __device__ __forceinline__ int warp_find_rank_bin(const int* hist, int nbins, in
   return bin;
 }
 
+// Adds one key's bin to this warp's private histogram; lanes of the warp
+// holding the same bin are combined first, so each bin sees one atomic per
+// warp instruction instead of a serialised run of same-address atomics.
+__device__ __forceinline__ void warp_hist_add(int* whist, int bin, bool active) {
+  const unsigned act = __ballot_sync(0xffffffffu, active);
+  if (!active) return;
+  const unsigned peers = __match_any_sync(act, bin);
+  if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&whist[bin], __popc(peers));
+}
+
+constexpr int kWarps = kTopkThreads / 32;
+
 __global__ void __launch_bounds__(kTopkThreads)
 topk_select_kernel(const uint16_t* __restrict__ s_all, int n, int k, int32_t* __restrict__ idx_all,
                    int64_t s_stride, int64_t idx_stride) {
   extern __shared__ __align__(16) uint16_t keys[];
-  __shared__ int hist1[256];
-  __shared__ int hist2[128];
+  __shared__ int whist[kWarps][256];  // per-warp histograms (level 1, then level 2)
+  __shared__ int hist[256];
   __shared__ int2 warp_tot[33];
   __shared__ unsigned s_max;
   __shared__ int s_nvalid;
-  __shared__ int s_sel[4];  // bin1, above1
+  __shared__ int s_sel[2];  // level-1 bin, count above it
   __shared__ float s_lohi[2];
 
   const uint16_t* s = s_all + blockIdx.x * s_stride;
   int32_t* idx = idx_all + blockIdx.x * idx_stride;
-  const int tid = threadIdx.x;
-  for (int i = tid; i < 256; i += kTopkThreads) hist1[i] = 0;
-  for (int i = tid; i < 128; i += kTopkThreads) hist2[i] = 0;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  int* mine = whist[warp];
+  for (int i = tid; i < kWarps * 256; i += kTopkThreads) (&whist[0][0])[i] = 0;
   if (tid == 0) { s_max = 0; s_nvalid = 0; }
   __syncthreads();
 
   pdl_wait();
   // Pass 1: magnitudes into shared memory, exponent histogram, max, count.
+  // Eight keys per thread per step (16-byte loads when s is 16-byte aligned).
   unsigned lmax = 0;
   int lvalid = 0;
-  for (int i = tid; i < n; i += kTopkThreads) {
-    uint16_t key = s[i] & 0x7FFF;
-    if (key > 0x7F80) key = kNanKey;  // NaN
-    keys[i] = key;
-    if (key != kNanKey) {
-      atomicAdd(&hist1[key >> 7], 1);
-      lmax = max(lmax, (unsigned)key);
-      ++lvalid;
+  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
+  const int nvec = vec ? n / 8 : 0;
+  const int steps = (nvec + kTopkThreads - 1) / kTopkThreads;
+  for (int st = 0; st < steps; ++st) {
+    const int v = st * kTopkThreads + tid;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (v < nvec) raw = __ldg(reinterpret_cast<const uint4*>(s) + v);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint16_t kk[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      uint16_t key = (uint16_t)((w[e >> 1] >> (16 * (e & 1))) & 0x7FFF);
+      if (key > 0x7F80) key = kNanKey;
+      kk[e] = key;
+      const bool ok = v < nvec && key != kNanKey;
+      if (ok) { lmax = max(lmax, (unsigned)key); ++lvalid; }
+      warp_hist_add(mine, key >> 7, ok);
     }
+    if (v < nvec) {
+      uint4 o;
+      o.x = kk[0] | ((uint32_t)kk[1] << 16);
+      o.y = kk[2] | ((uint32_t)kk[3] << 16);
+      o.z = kk[4] | ((uint32_t)kk[5] << 16);
+      o.w = kk[6] | ((uint32_t)kk[7] << 16);
+      reinterpret_cast<uint4*>(keys)[v] = o;
+    }
+  }
+  for (int base = nvec * 8; base < n; base += kTopkThreads) {  // scalar tail
+    const int i = base + tid;
+    uint16_t key = kNanKey;
+    if (i < n) {
+      key = s[i] & 0x7FFF;
+      if (key > 0x7F80) key = kNanKey;
+      keys[i] = key;
+    }
+    const bool ok = i < n && key != kNanKey;
+    if (ok) { lmax = max(lmax, (unsigned)key); ++lvalid; }
+    warp_hist_add(mine, key >> 7, ok);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -131,29 +173,46 @@ topk_select_kernel(const uint16_t* __restrict__ s_all, int n, int k, int32_t* __
     atomicAdd(&s_nvalid, lvalid);
   }
   __syncthreads();
+  if (tid < 256) {
+    int t = 0;
+#pragma unroll 8
+    for (int w = 0; w < kWarps; ++w) t += whist[w][tid];
+    hist[tid] = t;
+  }
+  __syncthreads();
   const int nvalid = s_nvalid;
   const bool has_w = nvalid >= k + 1;
 
   // Level 1 select: exponent byte of the (k+1)-th largest magnitude.
   if (has_w && tid < 32) {
     int above;
-    const int b = warp_find_rank_bin(hist1, 256, k + 1, &above);
+    const int b = warp_find_rank_bin(hist, 256, k + 1, &above);
     if (tid == 0) { s_sel[0] = b; s_sel[1] = above; }
   }
+  for (int i = tid; i < kWarps * 128; i += kTopkThreads) whist[i >> 7][i & 127] = 0;
   __syncthreads();
   if (has_w) {
     const int b1 = s_sel[0];
-    for (int i = tid; i < n; i += kTopkThreads) {
-      const uint16_t key = keys[i];
-      if (key != kNanKey && (key >> 7) == b1) atomicAdd(&hist2[key & 0x7F], 1);
+    for (int base = 0; base < n; base += kTopkThreads) {
+      const int i = base + tid;
+      const uint16_t key = i < n ? keys[i] : kNanKey;
+      const bool ok = key != kNanKey && (key >> 7) == b1;
+      warp_hist_add(mine, key & 0x7F, ok);
     }
+  }
+  __syncthreads();
+  if (tid < 128) {
+    int t = 0;
+#pragma unroll 8
+    for (int w = 0; w < kWarps; ++w) t += whist[w][tid];
+    hist[tid] = t;
   }
   __syncthreads();
   if (tid < 32) {
     float wv = 0.f;
     if (has_w) {
       int above2;
-      const int m = warp_find_rank_bin(hist2, 128, k + 1 - s_sel[1], &above2);
+      const int m = warp_find_rank_bin(hist, 128, k + 1 - s_sel[1], &above2);
       wv = bf16_bits_to_f32((unsigned)((s_sel[0] << 7) | m));
     }
     if (tid == 0) {
@@ -194,6 +253,30 @@ topk_select_kernel(const uint16_t* __restrict__ s_all, int n, int k, int32_t* __
   for (int i = filled + tid; i < k; i += kTopkThreads) idx[i] = 0;
 }
 
+// Shard selection for tensor parallelism along the intermediate dimension:
+// the entries of idx owned by this rank ([lo, hi)), in idx order, as local
+// row ids, and their number.
+__global__ void __launch_bounds__(kTopkThreads)
+shard_select_kernel(const int32_t* __restrict__ idx, int k, int lo, int hi,
+                    int32_t* __restrict__ local, int32_t* __restrict__ count) {
+  __shared__ int2 warp_tot[33];
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int per = (k + kTopkThreads - 1) / kTopkThreads;
+  const int beg = min(k, tid * per), end = min(k, beg + per);
+  int c = 0;
+  for (int j = beg; j < end; ++j) c += (idx[j] >= lo && idx[j] < hi);
+  int2 tot;
+  const int2 off = block_excl_scan2(c, 0, warp_tot, tot);
+  int pos = off.x;
+  for (int j = beg; j < end; ++j) {
+    const int v = idx[j];
+    if (v >= lo && v < hi) local[pos++] = v - lo;
+  }
+  pdl_launch_dependents();
+  if (tid == 0) count[0] = tot.x;
+}
+
 // Cache hit/miss split (dip_ca.py:137-142 with the src/row tables of
 // :164-171, misses pointing at the full resident rows).
 __global__ void __launch_bounds__(kTopkThreads)
@@ -230,7 +313,7 @@ int topk_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, int batch
   if (!s || (k > 0 && !idx)) return DIP_ERR_ARG;
   if (k == 0) return DIP_OK;
   const size_t smem = (size_t)n * 2;
-  if (smem > 48 * 1024) {
+  {  // static (~34 KB) + dynamic shared memory exceeds the 48 KB default
     cudaError_t e = cudaFuncSetAttribute(topk_select_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return launch_status(e);
@@ -264,4 +347,13 @@ extern "C" int dip_ca_split(const int32_t* idx, int64_t k, const int64_t* id2slo
   return launch_status(launch(ca_split_kernel, dim3(1), dim3(kTopkThreads), 0,
                               (cudaStream_t)stream, idx, (int)k, id2slot, n_channels,
                               combined_ids, src, row, n_hit));
+}
+
+extern "C" int dip_shard_select(const int32_t* idx, int64_t k, int64_t lo, int64_t hi,
+                                int32_t* local_idx, int32_t* count, dip_stream_t stream) {
+  if (k < 0 || k > INT32_MAX || lo < 0 || hi < lo || hi > INT32_MAX || !count) return DIP_ERR_ARG;
+  if (k > 0 && (!idx || !local_idx)) return DIP_ERR_ARG;
+  return launch_status(launch(shard_select_kernel, dim3(1), dim3(kTopkThreads), 0,
+                              (cudaStream_t)stream, idx, (int)k, (int)lo, (int)hi, local_idx,
+                              count));
 }

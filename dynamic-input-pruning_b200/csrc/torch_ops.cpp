@@ -350,6 +350,59 @@ Tensor residual_rmsnorm(const Tensor& y_in, const Tensor& r_in, double eps) {
   return out;
 }
 
+std::tuple<Tensor, Tensor> shard_select(const Tensor& idx_in, int64_t lo, int64_t hi) {
+  Tensor idx = idx32(idx_in, "idx");
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int64_t k = idx.numel();
+  auto iopt = idx.options().dtype(at::kInt);
+  Tensor local = at::empty({std::max<int64_t>(1, std::min<int64_t>(k, hi - lo))}, iopt);
+  Tensor count = at::empty({1}, iopt);
+  check_status(dip_shard_select(idx.data_ptr<int32_t>(), k, lo, hi, local.data_ptr<int32_t>(),
+                                count.data_ptr<int32_t>(), cur_stream()),
+               "shard_select");
+  return {local, count};
+}
+
+Tensor gather_up_h_count(const Tensor& up_qw, const Tensor& up_sc, const Tensor& x_in,
+                         const Tensor& g_in, const Tensor& idx_in, const Tensor& count) {
+  check_packed(up_qw, up_sc, "gather_up_h_count");
+  c10::cuda::CUDAGuard guard(up_qw.device());
+  Tensor x = x_in.contiguous(), g = g_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  check_dtype(g, at::kBFloat16, "g");
+  TORCH_CHECK(x.numel() == up_qw.size(1) * 2 && g.numel() == up_qw.size(0),
+              "gather_up_h_count: shape mismatch");
+  Tensor idx = idx32(idx_in, "idx");
+  check_dtype(count, at::kInt, "count");
+  Tensor h = bf16_empty(idx.numel(), x);
+  check_status(dip_gather_up_h_count(i8(up_qw), bf(up_sc), up_qw.size(0), bf(x), bf(g),
+                                     idx.data_ptr<int32_t>(), count.data_ptr<int32_t>(),
+                                     idx.numel(), up_qw.size(1) * 2, bfm(h), cur_stream()),
+               "gather_up_h_count");
+  return h;
+}
+
+Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& h_in,
+                           const Tensor& idx_in, const Tensor& count) {
+  check_packed(dt_qw, dt_sc, "gather_down_partial");
+  c10::cuda::CUDAGuard guard(dt_qw.device());
+  Tensor h = h_in.contiguous();
+  check_dtype(h, at::kBFloat16, "h");
+  Tensor idx = idx32(idx_in, "idx");
+  check_dtype(count, at::kInt, "count");
+  TORCH_CHECK(h.numel() == idx.numel(), "gather_down_partial: h/idx length mismatch");
+  const int64_t out_f = dt_qw.size(1) * 2;
+  Tensor y = at::empty({out_f}, h.options().dtype(at::kFloat));
+  Tensor ws = at::empty({(int64_t)dip_gather_down_workspace_bytes(out_f)},
+                        h.options().dtype(at::kByte));
+  check_status(dip_gather_down_partial(i8(dt_qw), bf(dt_sc), dt_qw.size(0), bf(h),
+                                       idx.data_ptr<int32_t>(), count.data_ptr<int32_t>(),
+                                       idx.numel(), out_f, ws.data_ptr(), ws.numel(),
+                                       y.data_ptr<float>(), cur_stream()),
+               "gather_down_partial");
+  return y;
+}
+
 int64_t op_set_pdl(int64_t enable) { return dip_set_pdl((int)enable); }
 
 }  // namespace
@@ -396,6 +449,13 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
   m.def("residual_rmsnorm(Tensor y, Tensor r, float eps) -> Tensor");
+  m.def("shard_select(Tensor idx, int lo, int hi) -> (Tensor, Tensor)");
+  m.def(
+      "gather_up_h_count(Tensor up_qw, Tensor up_sc, Tensor x, Tensor g, Tensor idx, "
+      "Tensor count) -> Tensor");
+  m.def(
+      "gather_down_partial(Tensor down_t_qw, Tensor down_t_sc, Tensor h, Tensor idx, "
+      "Tensor count) -> Tensor");
   m.def("set_pdl(int enable) -> int");
 }
 TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
@@ -411,5 +471,8 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("dequantize_int4", &dequantize_int4);
   m.impl("transpose_down_int4", &transpose_down_int4);
   m.impl("residual_rmsnorm", &residual_rmsnorm);
+  m.impl("shard_select", &shard_select);
+  m.impl("gather_up_h_count", &gather_up_h_count);
+  m.impl("gather_down_partial", &gather_down_partial);
 }
 TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) { m.impl("set_pdl", &op_set_pdl); }

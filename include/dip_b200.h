@@ -173,6 +173,25 @@ DIP_API int dip_transpose_down_int4(const int8_t* down_qw, const dip_bf16* down_
 DIP_API int dip_dequantize_int4_g128(const int8_t* qweight, const dip_bf16* scales, int64_t rows,
                              int64_t cols, dip_bf16* w, dip_stream_t stream);
 
+/* ---- tensor parallelism along the intermediate dimension (config 4) ----------
+ * Not in the reference (single GPU only).  Rank r owns channels [lo, hi) of
+ * gate, up and down_t.  After an all-gather of g every rank runs the same
+ * dip_topk_select; dip_shard_select keeps the selected channels it owns
+ * (local row ids, idx order) and their count on the device; the two kernels
+ * below take that device-side count (grids are sized for max_k) and the down
+ * projection returns fp32 partials for the all-reduce. */
+DIP_API int dip_shard_select(const int32_t* idx, int64_t k, int64_t lo, int64_t hi,
+                             int32_t* local_idx, int32_t* count, dip_stream_t stream);
+DIP_API int dip_gather_up_h_count(const int8_t* up_qw, const dip_bf16* up_sc, int64_t n_rows,
+                                  const dip_bf16* x, const dip_bf16* g, const int32_t* idx,
+                                  const int32_t* count, int64_t max_k, int64_t in_features,
+                                  dip_bf16* h, dip_stream_t stream);
+DIP_API int dip_gather_down_partial(const int8_t* down_t, const dip_bf16* scales,
+                                    int64_t n_rows, const dip_bf16* h, const int32_t* idx,
+                                    const int32_t* count, int64_t max_k, int64_t out_features,
+                                    void* workspace, size_t workspace_bytes, float* y_f32,
+                                    dip_stream_t stream);
+
 /* ---- inter-layer step of the synthetic decode stack ---------------------------
  * x_next = bf16(v * rsqrt(mean(v^2) + eps)), v = y + r (RMSNorm with unit
  * weight of a layer output plus a residual).  Not part of the reference's
