@@ -9,10 +9,26 @@
 
 namespace dip {
 
+__device__ unsigned int dip_error_word = 0;
+
 static std::atomic<int> g_pdl{1};
+static std::atomic<int> g_simple_gemv{0};
 static thread_local char g_last_err[256] = "";
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+bool force_simple_gemv() { return g_simple_gemv.load(std::memory_order_relaxed) != 0; }
+
+unsigned* error_word_ptr() {
+  static unsigned* cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, dip_error_word) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<unsigned*>(p);
+  }
+  return cache[dev];
+}
 
 int launch_status(cudaError_t e) {
   if (e == cudaSuccess) return DIP_OK;
@@ -21,9 +37,12 @@ int launch_status(cudaError_t e) {
 }
 
 int num_sms() {
+  static int cache[64] = {};
   int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev]) return cache[dev];
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  cache[dev] = n;
   return n;
 }
 
@@ -50,6 +69,16 @@ extern "C" const char* dip_status_string(int status) {
 extern "C" const char* dip_last_cuda_error(void) { return g_last_err; }
 
 extern "C" int dip_set_pdl(int enable) { return g_pdl.exchange(enable ? 1 : 0); }
+
+extern "C" int dip_set_gemv_variant(int simple) { return g_simple_gemv.exchange(simple ? 1 : 0); }
+
+extern "C" int dip_take_device_error(unsigned int* out) {
+  if (!out) return DIP_ERR_ARG;
+  unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(out, dip_error_word, sizeof(unsigned int));
+  if (e != cudaSuccess) return launch_status(e);
+  return launch_status(cudaMemcpyToSymbol(dip_error_word, &zero, sizeof(unsigned int)));
+}
 
 extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k < 0) return 0;

@@ -37,11 +37,17 @@ __device__ __forceinline__ float round_bf16(float f) {
 // 16-bit lane below holds exactly  128 + (q + 8) = q + 136  with q in [-8,7].
 // Lane pairing: out[p] = (nibble p, nibble p+4) for p = 0..3.
 constexpr float kNibbleBias = 136.0f;
+// (a & 0x000F000F) ^ 0x43084308 as a single LOP3 (lookup table 0x6a).
+__device__ __forceinline__ uint32_t nib_lop3(uint32_t a) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x43084308, 0x6a;\n" : "=r"(d) : "r"(a));
+  return d;
+}
 __device__ __forceinline__ void nib8_biased_bf16x2(uint32_t w, uint32_t (&o)[4]) {
-  o[0] = (w & 0x000F000Fu) ^ 0x43084308u;
-  o[1] = ((w >> 4) & 0x000F000Fu) ^ 0x43084308u;
-  o[2] = ((w >> 8) & 0x000F000Fu) ^ 0x43084308u;
-  o[3] = ((w >> 12) & 0x000F000Fu) ^ 0x43084308u;
+  o[0] = nib_lop3(w);
+  o[1] = nib_lop3(w >> 4);
+  o[2] = nib_lop3(w >> 8);
+  o[3] = nib_lop3(w >> 12);
 }
 
 // Same idea in fp32: 2^23 = 0x4B000000 has a mantissa step of 1, so
@@ -114,4 +120,70 @@ cudaError_t launch(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
 
 int num_sms();
 
+// Test switch: route the GEMV family through the simple (non-ring) kernel.
+bool force_simple_gemv();
+
+// Device address of the library's error word on the current device (looked
+// up once per device with cudaGetSymbolAddress); nullptr on failure.
+unsigned* error_word_ptr();
+
+}  // namespace dip
+
+namespace dip {
+// ---------------------------------------------------------------------------
+// mbarrier + bulk-copy (TMA, non-tensor, no multicast) helpers.  Every wait
+// is bounded: after kSpinLimit polls it ORs an error code into the device
+// error word (a kernel argument, see error_word_ptr) and reports failure
+// instead of hanging.
+constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr unsigned kErrTimeout = 1u;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and flags the error) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(err, kErrTimeout);
+  return false;
+}
+// Global -> shared bulk copy completing on an mbarrier (size % 16 == 0,
+// both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Named barrier for a subset of warps (id 1..15).
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
 }  // namespace dip

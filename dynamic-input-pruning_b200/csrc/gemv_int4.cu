@@ -224,10 +224,260 @@ gemv_int4_kernel(const GemvParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent ring variant (used when in_features % 1024 == 0 and the ring
+// fits in shared memory).  One CTA per SM: warp 8 is the producer, streaming
+// 16-row tiles (every row as one bulk copy, plus its scales) into a 4-stage
+// shared-memory ring with cp.async.bulk + mbarrier completion; warps 0..7
+// consume, each owning a fixed K-slice of GW groups whose x fragments stay in
+// registers for the whole kernel.  Rows are stored with a 16-byte pad so the
+// 128-bit shared loads of rows g and g+8 fall in different banks.  In the
+// dense mode the producer issues its first copies before waiting on the
+// predecessor kernel (weights are static), overlapping the previous launch.
+constexpr int kRingConsumers = 8;
+constexpr int kRingThreads = (kRingConsumers + 1) * 32;
+constexpr int kRingStages = 4;
+constexpr int kRingPad = 16;
+
+struct RingGeom {
+  int rowb, scb, row_stride, stage_bytes, x_off, gsum_off, red_off, bar_off, total;
+};
+__host__ __device__ inline RingGeom ring_geom(int in) {
+  RingGeom g;
+  const int G = in / kGroup;
+  g.rowb = in / 2;
+  g.scb = G * 2;
+  g.row_stride = g.rowb + kRingPad;
+  g.stage_bytes = 16 * g.row_stride + 16 * g.scb;
+  g.stage_bytes = (g.stage_bytes + 127) & ~127;
+  g.x_off = kRingStages * g.stage_bytes;
+  g.gsum_off = g.x_off + in * 2;
+  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
+  g.bar_off = g.red_off + 2 * kRingConsumers * 16 * 4;
+  g.total = g.bar_off + 2 * kRingStages * 8;
+  return g;
+}
+
+__device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb, const uint32_t* bw,
+                                          float (&d0)[4], float (&d1)[4]) {
+  const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t rb[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint32_t qa4[4], qb4[4];
+    nib8_biased_bf16x2(ra[w], qa4);
+    nib8_biased_bf16x2(rb[w], qb4);
+    const uint32_t a_even[4] = {qa4[0], qb4[0], qa4[1], qb4[1]};
+    const uint32_t a_odd[4] = {qa4[2], qb4[2], qa4[3], qb4[3]};
+    mma_bf16_16816(d0, a_even, bw[4 * w + 0], bw[4 * w + 1]);
+    mma_bf16_16816(d1, a_odd, bw[4 * w + 2], bw[4 * w + 3]);
+  }
+}
+
+template <int MODE, int EPI, int GW>
+__global__ void __launch_bounds__(kRingThreads, 1)
+gemv_ring_kernel(const GemvParams p, unsigned* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int in = p.in_features;
+  const int G = in / kGroup;
+  const RingGeom geo = ring_geom(in);
+  uint32_t* xstage = reinterpret_cast<uint32_t*>(smem + geo.x_off);
+  float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
+  float* red = reinterpret_cast<float*>(smem + geo.red_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + geo.bar_off);
+  uint64_t* empty = full + kRingStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRingStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (MODE != ROW_DENSE) pdl_wait();
+  int n_out = p.n_out;
+  if (p.count) n_out = min(n_out, *p.count);
+  const int nt = (n_out + 15) / 16;
+  const int t0 = (int)((int64_t)nt * blockIdx.x / gridDim.x);
+  const int t1 = (int)((int64_t)nt * (blockIdx.x + 1) / gridDim.x);
+  const int ntile = t1 - t0;
+
+  if (warp == kRingConsumers) {
+    // ---------------- producer ----------------
+    bool ok = true;
+    for (int i = 0; i < ntile && ok; ++i) {
+      const int s = i % kRingStages;
+      const uint32_t par = ((i / kRingStages) & 1) ^ 1;
+      if (lane == 0) ok = mbar_wait(&empty[s], par, err);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const int r0 = (t0 + i) * 16;
+      const int rows = min(16, n_out - r0);
+      uint8_t* st = smem + s * geo.stage_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], rows * (geo.rowb + geo.scb));
+      __syncwarp();
+      if (lane < rows) {
+        const uint8_t* qw;
+        const uint16_t* sc;
+        resolve_row<MODE>(p, r0 + lane, qw, sc);
+        bulk_g2s(st + lane * geo.row_stride, qw, geo.rowb, &full[s]);
+        bulk_g2s(st + 16 * geo.row_stride + lane * geo.scb, sc, geo.scb, &full[s]);
+      }
+    }
+    // Do not leave with copies in flight: wait (bounded) for the last stages.
+    if (lane == 0 && ok) {
+      for (int i = max(0, ntile - kRingStages); i < ntile; ++i)
+        if (!mbar_wait(&full[i % kRingStages], (i / kRingStages) & 1, err)) break;
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int ctid = threadIdx.x;  // 0..255
+  const int gq = lane >> 2, tq = lane & 3;
+  if (MODE == ROW_DENSE) pdl_wait();
+  {
+    const int nwords = in / 8;
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+    for (int wi = ctid; wi < ((nwords + 255) & ~255); wi += kRingConsumers * 32) {
+      float part = 0.f;
+      if (wi < nwords) {
+        const uint4 v = __ldg(xv + wi);
+        uint4 o;
+        o.x = __byte_perm(v.x, v.z, 0x5410);
+        o.y = __byte_perm(v.x, v.z, 0x7632);
+        o.z = __byte_perm(v.y, v.w, 0x5410);
+        o.w = __byte_perm(v.y, v.w, 0x7632);
+        reinterpret_cast<uint4*>(xstage)[wi] = o;
+        part = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) +
+               bf16_bits_to_f32(v.y & 0xFFFF) + bf16_bits_to_f32(v.y >> 16) +
+               bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
+               bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 8);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
+    }
+  }
+  named_bar(1, kRingConsumers * 32);
+  const int g0 = warp * GW;
+  uint32_t xf[GW][16];
+  float bias[GW];
+#pragma unroll
+  for (int gi = 0; gi < GW; ++gi) {
+    const int grp = min(g0 + gi, G - 1);
+    const uint4* bp = reinterpret_cast<const uint4*>(xstage + grp * 64 + tq * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 b = bp[q];
+      xf[gi][4 * q + 0] = b.x; xf[gi][4 * q + 1] = b.y;
+      xf[gi][4 * q + 2] = b.z; xf[gi][4 * q + 3] = b.w;
+    }
+    bias[gi] = kNibbleBias * gsum[grp];
+  }
+
+  bool ok = true;
+  for (int i = 0; i < ntile; ++i) {
+    const int s = i % kRingStages;
+    if (ok) ok = mbar_wait(&full[s], (i / kRingStages) & 1, err);
+    const uint8_t* st = smem + s * geo.stage_bytes;
+    const uint8_t* rowa = st + gq * geo.row_stride;
+    const uint8_t* rowbp = st + (gq + 8) * geo.row_stride;
+    const uint16_t* sca = reinterpret_cast<const uint16_t*>(st + 16 * geo.row_stride + gq * geo.scb);
+    const uint16_t* scbp = reinterpret_cast<const uint16_t*>(st + 16 * geo.row_stride +
+                                                             (gq + 8) * geo.scb);
+    float acc_a = 0.f, acc_b = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int gi = 0; gi < GW; ++gi) {
+        const int grp = g0 + gi;
+        if (grp < G) {
+          const uint4 wa = *reinterpret_cast<const uint4*>(rowa + grp * kGroupBytes + tq * 16);
+          const uint4 wb = *reinterpret_cast<const uint4*>(rowbp + grp * kGroupBytes + tq * 16);
+          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+          group_mma(wa, wb, xf[gi], d0, d1);
+          acc_a = fmaf(bf16_bits_to_f32(sca[grp]), (d0[0] + d1[0]) - bias[gi], acc_a);
+          acc_b = fmaf(bf16_bits_to_f32(scbp[grp]), (d0[2] + d1[2]) - bias[gi], acc_b);
+        }
+      }
+    }
+    float* rr = red + (i & 1) * kRingConsumers * 16;
+    if (tq == 0) {
+      rr[warp * 16 + gq] = acc_a;
+      rr[warp * 16 + gq + 8] = acc_b;
+    }
+    named_bar(1, kRingConsumers * 32);
+    if (ctid == 0) mbar_arrive(&empty[s]);
+    if (warp == 0 && lane < 16) {
+      const int j = (t0 + i) * 16 + lane;
+      if (j < n_out && ok) {
+        float v = rr[lane];
+#pragma unroll
+        for (int w = 1; w < kRingConsumers; ++w) v += rr[w * 16 + lane];
+        const uint8_t* dq;
+        const uint16_t* ds;
+        const bool valid = resolve_row<MODE>(p, j, dq, ds);
+        uint16_t o;
+        if (!valid) o = 0;
+        else if (EPI == EPI_PLAIN) o = f32_to_bf16_bits(v);
+        else if (EPI == EPI_SILU) o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+        else o = f32_to_bf16_bits(bf16_bits_to_f32(p.g[p.gid[j]]) * round_bf16(v));
+        p.out[j] = o;
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+template <int MODE, int EPI, int GW>
+static int launch_ring(const GemvParams& p, cudaStream_t s) {
+  const RingGeom geo = ring_geom(p.in_features);
+  auto kern = gemv_ring_kernel<MODE, EPI, GW>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       geo.total);
+  if (e != cudaSuccess) return launch_status(e);
+  const int nt = (p.n_out + 15) / 16;
+  const int grid = nt < num_sms() ? nt : num_sms();
+  unsigned* err = error_word_ptr();
+  if (!err) return DIP_ERR_CUDA;
+  return launch_status(launch(kern, dim3(grid), dim3(kRingThreads), (size_t)geo.total, s, p, err));
+}
+
+// The ring kernel needs whole 8-group K-slices (G % 8 == 0) so every row's
+// scales are a 16-byte multiple, and its ring must fit in shared memory.
+static bool ring_ok(const GemvParams& p) {
+  const int G = p.in_features / kGroup;
+  if (G % 8 != 0 || G / 8 > 8) return false;
+  if (ring_geom(p.in_features).total > 220 * 1024) return false;
+  if ((reinterpret_cast<uintptr_t>(p.sc0) & 15) != 0) return false;
+  if (p.qw1 && (reinterpret_cast<uintptr_t>(p.sc1) & 15) != 0) return false;
+  return true;
+}
+
+template <int MODE, int EPI>
+static int launch_ring_any(const GemvParams& p, cudaStream_t s) {
+  switch (p.in_features / kGroup / 8) {
+    case 1: return launch_ring<MODE, EPI, 1>(p, s);
+    case 2: return launch_ring<MODE, EPI, 2>(p, s);
+    case 3: return launch_ring<MODE, EPI, 3>(p, s);
+    case 4: return launch_ring<MODE, EPI, 4>(p, s);
+    case 5: return launch_ring<MODE, EPI, 5>(p, s);
+    case 6: return launch_ring<MODE, EPI, 6>(p, s);
+    case 7: return launch_ring<MODE, EPI, 7>(p, s);
+    default: return launch_ring<MODE, EPI, 8>(p, s);
+  }
+}
+
 // Host launcher shared by the entry points below.
 template <int MODE, int EPI>
 static int launch_gemv(const GemvParams& p, cudaStream_t s) {
   if (p.n_out == 0) return DIP_OK;
+  if (ring_ok(p) && !force_simple_gemv()) return launch_ring_any<MODE, EPI>(p, s);
   const int G = p.in_features / kGroup;
   const size_t smem = (size_t)p.in_features * 2 + (size_t)G * 4 + kGemvWarps * 16 * 4;
   auto kern = gemv_int4_kernel<MODE, EPI>;

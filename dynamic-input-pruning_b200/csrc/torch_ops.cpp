@@ -404,6 +404,12 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
 }
 
 int64_t op_set_pdl(int64_t enable) { return dip_set_pdl((int)enable); }
+int64_t op_set_gemv_variant(int64_t simple) { return dip_set_gemv_variant((int)simple); }
+int64_t op_take_device_error() {
+  unsigned int v = 0;
+  check_status(dip_take_device_error(&v), "take_device_error");
+  return (int64_t)v;
+}
 
 }  // namespace
 
@@ -457,6 +463,8 @@ TORCH_LIBRARY(dip_b200, m) {
       "gather_down_partial(Tensor down_t_qw, Tensor down_t_sc, Tensor h, Tensor idx, "
       "Tensor count) -> Tensor");
   m.def("set_pdl(int enable) -> int");
+  m.def("set_gemv_variant(int simple) -> int");
+  m.def("take_device_error() -> int");
 }
 TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("gate_silu", &gate_silu);
@@ -475,4 +483,8 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("gather_up_h_count", &gather_up_h_count);
   m.impl("gather_down_partial", &gather_down_partial);
 }
-TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) { m.impl("set_pdl", &op_set_pdl); }
+TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) {
+  m.impl("set_pdl", &op_set_pdl);
+  m.impl("set_gemv_variant", &op_set_gemv_variant);
+  m.impl("take_device_error", &op_take_device_error);
+}

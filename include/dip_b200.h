@@ -51,6 +51,16 @@ DIP_API const char* dip_last_cuda_error(void);
 /* Enable (1) / disable (0) programmatic dependent launch between the kernels
  * of one call chain.  Default 1.  Returns the previous setting. */
 DIP_API int dip_set_pdl(int enable);
+/* Reads and clears the device error word of the current device: bit 0 set
+ * means a kernel gave up a bounded wait (a pipeline barrier that never
+ * completed) and returned early; its outputs are then invalid.  Synchronous
+ * (a device-to-host copy).  0 = no error recorded. */
+DIP_API int dip_take_device_error(unsigned int* out);
+/* Selects the GEMV implementation: 0 (default) = persistent bulk-copy ring
+ * kernel where the shape allows it, 1 = the simple one-tile-per-CTA kernel.
+ * Both give the same values up to fp32 summation order; the switch exists
+ * for testing and comparison.  Returns the previous setting. */
+DIP_API int dip_set_gemv_variant(int simple);
 
 /* ---- a5/a6: int4 GEMV, optionally fused with SiLU --------------------------
  * out[r] = bf16(sum_c q[r,c]*s[r,c/128]*x[c]); with apply_silu != 0 the result

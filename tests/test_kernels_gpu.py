@@ -238,3 +238,35 @@ def test_ca_split_exact(dip, oracle, dev):
     rc, rs, rr, rn = oracle.ca_split(idx, id2slot)
     assert torch.equal(comb.cpu(), rc) and torch.equal(src.cpu(), rs)
     assert torch.equal(row.cpu(), rr) and nh.item() == rn
+
+
+# ---------------------------------------------------------------- GEMV variants
+@pytest.mark.parametrize("in_f", [1024, 2048, 5120])
+@pytest.mark.parametrize("rows", [7, 16, 300, 4097])
+def test_ring_and_simple_gemv_agree(dip, oracle, dev, in_f, rows):
+    """The persistent bulk-copy ring kernel and the simple kernel give the same
+    values (up to fp32 summation order) in every row mode and epilogue, and
+    both match the oracle."""
+    gen = torch.Generator().manual_seed(rows + in_f)
+    qw, sc = rand_packed(rows, in_f, gen, oracle)
+    x = torch.randn(in_f, generator=gen).to(torch.bfloat16)
+    g = torch.randn(rows, generator=gen).to(torch.bfloat16)
+    k = max(1, rows // 2)
+    idx = torch.randperm(rows, generator=gen)[:k].to(torch.int32)
+    d = [t.to(dev) for t in (qw, sc, x, g, idx)]
+    outs = []
+    for simple in (0, 1):
+        prev = torch.ops.dip_b200.set_gemv_variant(simple)
+        try:
+            outs.append((torch.ops.dip_b200.gate_silu(d[0], d[1], d[2]).cpu(),
+                         torch.ops.int4_gather_ops.int4_gather_gemv(d[0], d[1], d[2], d[4]).cpu(),
+                         torch.ops.dip_b200.gather_up_h(d[0], d[1], d[2], d[3], d[4]).cpu()))
+        finally:
+            torch.ops.dip_b200.set_gemv_variant(prev)
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    ref_full = oracle.int4_gemv_f32(qw, sc, x)
+    for a, b in zip(*outs):
+        close(a, b)
+    close(outs[0][0], oracle.silu_bf16(ref_full.to(torch.bfloat16)))
+    close(outs[0][1], ref_full[idx.long()])
