@@ -174,6 +174,207 @@ reduce_partials_kernel(const float* __restrict__ partial, int nparts, int out,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core variant (used when out % 1024 == 0 and out <= 5120).
+//
+//   y[o] = sum_c q[c,o] * (h_c * s[c, o/128])
+//
+// is computed as D[o][n] = sum_c A[o][c] * B[c][n] with mma.sync m16n8k16:
+// A = the int4 weights (outputs on M, channels on K) converted in registers
+// to bf16 q+136 (magic number, see nib8_biased_bf16x2); two channel rows are
+// interleaved byte-wise with one PRMT so each 32-bit register holds the same
+// output of two channels.  B holds hs = h*s split exactly into bf16 hi + lo:
+// even columns carry hi, odd columns lo, so D[o][2t] + D[o][2t+1] is the sum
+// over channels of q*hs (+136 * sum hs, removed with the column sums at the
+// end).  The tensor core therefore does both the multiply-adds and the
+// channel reduction; a lane spends ~1.2 instructions per weight nibble.
+//
+// Grid: 2 output halves x S channel slices.  Each CTA streams, for its
+// slice, the half rows (out/4 bytes) plus the scale row of 16 channels per
+// stage into an 8-stage shared-memory ring with cp.async.bulk (producer warp)
+// and has out/256 consumer warps, warp w owning output group w of the half
+// (64 bytes of every row, 8 accumulator m-tiles = 32 fp32 registers).
+constexpr int kDmStages = 8;
+constexpr int kDmChan = 16;       // channels per stage (one MMA K step)
+constexpr int kDmSlices = 74;     // channel slices; 2 x 74 = 148 CTAs
+constexpr int kDmPad = 16;
+
+struct DmGeom {
+  int half_bytes, row_stride, scb, stage_bytes, h_off, bar_off, total;
+};
+__host__ __device__ inline DmGeom dm_geom(int out, int max_slice) {
+  DmGeom g;
+  g.half_bytes = out / 4;
+  g.row_stride = g.half_bytes + kDmPad;
+  g.scb = (out / kGroup) * 2;
+  g.stage_bytes = (kDmChan * g.row_stride + kDmChan * g.scb + 127) & ~127;
+  g.h_off = kDmStages * g.stage_bytes;
+  g.bar_off = g.h_off + ((max_slice * 4 + 15) & ~15);
+  g.total = g.bar_off + 2 * kDmStages * 8;
+  return g;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(672, 1)
+down_mma_kernel(const DownParams p, int max_slice, unsigned* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int out = p.out_features;
+  const int nwarps = out / 256;  // consumer warps
+  const DmGeom geo = dm_geom(out, max_slice);
+  float* hsm = reinterpret_cast<float*>(smem + geo.h_off);  // h of the slice (fp32)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + geo.bar_off);
+  uint64_t* empty = full + kDmStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = blockIdx.x & 1, slice = blockIdx.x >> 1, nslices = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], nwarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  int k = p.k;
+  if (p.count) k = min(k, *p.count);
+  const int j0 = (int)((int64_t)k * slice / nslices);
+  const int j1 = (int)((int64_t)k * (slice + 1) / nslices);
+  const int nstage = (j1 - j0 + kDmChan - 1) / kDmChan;
+
+  if (warp == nwarps) {
+    // ---------------- producer ----------------
+    bool ok = true;
+    for (int i = 0; i < nstage && ok; ++i) {
+      const int s = i % kDmStages;
+      if (lane == 0) ok = mbar_wait(&empty[s], ((i / kDmStages) & 1) ^ 1, err);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const int c0 = j0 + i * kDmChan;
+      const int rows = min(kDmChan, j1 - c0);
+      uint8_t* st = smem + s * geo.stage_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], rows * (geo.half_bytes + geo.scb));
+      __syncwarp();
+      if (lane < rows) {
+        const uint8_t* qw;
+        const uint16_t* sc;
+        down_row<MODE>(p, c0 + lane, qw, sc);
+        bulk_g2s(st + lane * geo.row_stride, qw + half * geo.half_bytes, geo.half_bytes,
+                 &full[s]);
+        bulk_g2s(st + kDmChan * geo.row_stride + lane * geo.scb, sc, geo.scb, &full[s]);
+      }
+    }
+    if (lane == 0 && ok) {
+      for (int i = max(0, nstage - kDmStages); i < nstage; ++i)
+        if (!mbar_wait(&full[i % kDmStages], (i / kDmStages) & 1, err)) break;
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  // h of this slice (0 for channels whose row index is out of range).
+  for (int j = j0 + threadIdx.x; j < j1; j += nwarps * 32) {
+    const uint8_t* qw;
+    const uint16_t* sc;
+    const bool okr = down_row<MODE>(p, j, qw, sc);
+    hsm[j - j0] = okr ? bf16_bits_to_f32(p.h[j]) : 0.f;
+  }
+  named_bar(1, nwarps * 32);
+
+  const int gq = lane >> 2, tq = lane & 3;
+  const int og = half * nwarps + warp;  // global output group of this warp
+  // Table lane mapping: lanes 0..15 -> (pair = lane & 7, which = lane >> 3).
+  const int tpair = lane & 7, twhich = (lane >> 3) & 1;
+  float acc[8][4];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+  float colsum = 0.f;
+  bool ok = true;
+  for (int i = 0; i < nstage; ++i) {
+    const int s = i % kDmStages;
+    if (ok) ok = mbar_wait(&full[s], (i / kDmStages) & 1, err);
+    const uint8_t* st = smem + s * geo.stage_bytes;
+    const int c0 = i * kDmChan;  // slice-local channel of row 0
+    const int rows = min(kDmChan, j1 - j0 - c0);
+    // B values: lane (pair, which) packs channels 2*pair, 2*pair+1 of this
+    // stage as bf16x2 of hi (which 0) or lo (which 1) of h*s.
+    uint32_t bval = 0;
+    if (lane < 16) {
+      float v2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 2 * tpair + e;
+        float hs = 0.f;
+        if (c < rows) {
+          const uint16_t* sc =
+              reinterpret_cast<const uint16_t*>(st + kDmChan * geo.row_stride + c * geo.scb);
+          hs = hsm[c0 + c] * bf16_bits_to_f32(sc[og]);
+        }
+        const float hi = round_bf16(hs);
+        v2[e] = twhich ? round_bf16(hs - hi) : hi;
+      }
+      colsum += v2[0] + v2[1];
+      bval = (uint32_t)f32_to_bf16_bits(v2[0]) | ((uint32_t)f32_to_bf16_bits(v2[1]) << 16);
+    }
+    const int src = (gq & 1) * 8;
+    const uint32_t b0 = __shfl_sync(0xffffffffu, bval, src + tq);
+    const uint32_t b1 = __shfl_sync(0xffffffffu, bval, src + tq + 4);
+    if (ok) {
+      // rows 2t, 2t+1, 2t+8, 2t+9 of the stage, bytes [64*warp + 8*g, +8)
+      const int boff = warp * 64 + gq * 8;
+      const uint2 ra = *reinterpret_cast<const uint2*>(st + (2 * tq) * geo.row_stride + boff);
+      const uint2 rb = *reinterpret_cast<const uint2*>(st + (2 * tq + 1) * geo.row_stride + boff);
+      const uint2 rc = *reinterpret_cast<const uint2*>(st + (2 * tq + 8) * geo.row_stride + boff);
+      const uint2 rd = *reinterpret_cast<const uint2*>(st + (2 * tq + 9) * geo.row_stride + boff);
+      const uint32_t pab[4] = {__byte_perm(ra.x, rb.x, 0x5410), __byte_perm(ra.x, rb.x, 0x7632),
+                               __byte_perm(ra.y, rb.y, 0x5410), __byte_perm(ra.y, rb.y, 0x7632)};
+      const uint32_t pcd[4] = {__byte_perm(rc.x, rd.x, 0x5410), __byte_perm(rc.x, rd.x, 0x7632),
+                               __byte_perm(rc.y, rd.y, 0x5410), __byte_perm(rc.y, rd.y, 0x7632)};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t xa[4], xc[4];
+        nib8_biased_bf16x2(pab[q], xa);
+        nib8_biased_bf16x2(pcd[q], xc);
+        // m-tile 2q: byte 2q of the lane's 8 (low nibble -> row g, high -> g+8)
+        const uint32_t a0[4] = {xa[0], xa[1], xc[0], xc[1]};
+        const uint32_t a1[4] = {xa[2], xa[3], xc[2], xc[3]};
+        mma_bf16_16816(acc[2 * q], a0, b0, b1);
+        mma_bf16_16816(acc[2 * q + 1], a1, b0, b1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  pdl_launch_dependents();
+  // Column sums of hi (lanes 0..7) and lo (lanes 8..15) -> their total.
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) colsum += __shfl_xor_sync(0xffffffffu, colsum, o);
+  const float bias = kNibbleBias * __shfl_sync(0xffffffffu, colsum, 0);
+  if (tq == 0) {
+    // lane g holds outputs 16g .. 16g+15 of the group: m-tile m -> byte m,
+    // row g -> low nibble (even output), row g+8 -> high nibble (odd).
+    float* dst = p.partial + (size_t)slice * out + og * kGroup + gq * 16;
+    float v[16];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      v[2 * m] = ok ? acc[m][0] + acc[m][1] - bias : 0.f;
+      v[2 * m + 1] = ok ? acc[m][2] + acc[m][3] - bias : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
+                                                      v[4 * q + 3]);
+  }
+}
+
+static bool dm_ok(const DownParams& p) {
+  const int out = p.out_features;
+  if (out % 1024 != 0 || out / 256 > 20) return false;
+  if ((reinterpret_cast<uintptr_t>(p.sc0) & 15) != 0) return false;
+  if (p.qw1 && (reinterpret_cast<uintptr_t>(p.sc1) & 15) != 0) return false;
+  return true;
+}
+
 size_t down_workspace_bytes(int64_t out) { return (size_t)kDownCtas * out * sizeof(float); }
 
 bool down_shape_ok(int64_t out) { return out > 0 && out % kGroup == 0 && out / 32 <= 640; }
@@ -184,6 +385,24 @@ int launch_down(DownParams p, uint16_t* y, float* y_f32, void* ws, size_t ws_byt
   const int out = p.out_features;
   if (ws_bytes < down_workspace_bytes(out) || !ws) return DIP_ERR_WORKSPACE;
   p.partial = reinterpret_cast<float*>(ws);
+  if (dm_ok(p) && !force_simple_gemv() && p.k > 0) {
+    const int nsl = p.k < kDmSlices ? p.k : kDmSlices;
+    const int max_slice = (p.k + nsl - 1) / nsl + 1;
+    const DmGeom geo = dm_geom(out, max_slice);
+    if (geo.total <= 220 * 1024) {
+      auto kern = down_mma_kernel<MODE>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           geo.total);
+      if (e != cudaSuccess) return launch_status(e);
+      unsigned* err = error_word_ptr();
+      if (!err) return DIP_ERR_CUDA;
+      int st1 = launch_status(launch(kern, dim3(2 * nsl), dim3((out / 256 + 1) * 32),
+                                     (size_t)geo.total, st, p, max_slice, err));
+      if (st1 != DIP_OK) return st1;
+      return launch_status(launch(reduce_partials_kernel, dim3((out + 31) / 32), dim3(256), 0,
+                                  st, (const float*)p.partial, nsl, out, y, y_f32));
+    }
+  }
   const int nch = out / 32;
   int teams = 640 / nch;
   if (teams > 4) teams = 4;

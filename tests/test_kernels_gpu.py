@@ -270,3 +270,27 @@ def test_ring_and_simple_gemv_agree(dip, oracle, dev, in_f, rows):
         close(a, b)
     close(outs[0][0], oracle.silu_bf16(ref_full.to(torch.bfloat16)))
     close(outs[0][1], ref_full[idx.long()])
+
+
+@pytest.mark.parametrize("out_f", [1024, 5120])
+@pytest.mark.parametrize("k", [1, 15, 16, 17, 300, 15360])
+def test_down_variants_agree(dip, oracle, dev, out_f, k):
+    """Tensor-core (ring) and CUDA-core down projections agree and match the
+    oracle, with idx gather, the staged (identity) layout and odd k."""
+    gen = torch.Generator().manual_seed(out_f + k)
+    n = max(k, 64)
+    dtw, sc = rand_packed(n, out_f, gen, oracle)
+    h = torch.randn(k, generator=gen).to(torch.bfloat16)
+    idx = torch.randperm(n, generator=gen)[:k].to(torch.int32)
+    ys = []
+    for simple in (0, 1):
+        prev = torch.ops.dip_b200.set_gemv_variant(simple)
+        try:
+            ys.append(torch.ops.dip_b200.gather_down_idx(dtw.to(dev), sc.to(dev), h.to(dev),
+                                                         idx.to(dev)).cpu())
+        finally:
+            torch.ops.dip_b200.set_gemv_variant(prev)
+    assert torch.ops.dip_b200.take_device_error() == 0
+    ref = oracle.gather_down_f32(dtw, sc, h, rows=idx.long())
+    close(ys[0], ref)
+    close(ys[1], ref)

@@ -103,3 +103,16 @@ def test_small_layer_forward_consistency(oracle):
     wd = oracle.dequantize(L["down_t_qw"], L["down_t_sc"]).double()
     ref = r["h"].double() @ wd[r["idx"].long()]
     assert torch.allclose(r["y_f32"].double(), ref, rtol=1e-2, atol=2e-3)
+
+
+TOPK_GOLDEN = Path(__file__).with_name("golden") / "topk_ref_golden.pt"
+
+
+def test_topk_oracle_matches_reference_kernel_vectors(oracle):
+    """Vectors produced by the reference's own topk_select.cu (compiled from
+    its source for sm_100a and run on a B200 by tests/test_ref_kernels_gpu.py
+    with DIP_WRITE_GOLDEN set): the literal CPU restatement reproduces them."""
+    cases = torch.load(TOPK_GOLDEN)
+    assert len(cases) >= 8
+    for name, c in cases.items():
+        assert torch.equal(oracle.topk_select(c["s"], c["k"]), c["idx"]), name
