@@ -509,3 +509,45 @@ extern "C" int dip_gather_down_partial(const int8_t* down_t, const dip_bf16* sca
   return launch_down<DROW_GATHER>(p, nullptr, y_f32, workspace, workspace_bytes,
                                   (cudaStream_t)stream);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free down projection.
+//
+// Some callers cannot allocate device memory at call time: code running
+// inside another framework's memory pool or under a fixed memory budget,
+// plugins that are handed only input and output buffers, and C / FFI callers
+// without a CUDA allocator of their own.  For them this entry point keeps the
+// per-CTA partial sums in a library-owned static device array instead of a
+// caller workspace.  The array lives in every GPU that loads the library
+// until the process exits.
+constexpr int64_t kNoAllocMaxOut = 8192;  // largest supported out_features
+static __device__ __align__(256) float g_noalloc_partials[kDownCtas * kNoAllocMaxOut];
+
+// Device address of g_noalloc_partials on the current device.  In host code
+// the array's name is only a host-side stand-in, so the real address is
+// looked up once per device (with that device current) and cached.
+static float* noalloc_partials_ptr() {
+  static float* cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_partials) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<float*>(ptr);
+  }
+  return cache[dev];
+}
+
+extern "C" int dip_int4_gather_down_noalloc(const int8_t* down_t, const dip_bf16* scales,
+                                            int64_t n_rows, const dip_bf16* h,
+                                            const int32_t* idx, int64_t k, int64_t out_features,
+                                            dip_bf16* y, dip_stream_t stream) {
+  if (out_features > kNoAllocMaxOut) return DIP_ERR_UNSUPPORTED;
+  float* scratch = noalloc_partials_ptr();
+  if (!scratch) {
+    launch_status(cudaGetLastError());  // records the CUDA error text
+    return DIP_ERR_CUDA;
+  }
+  return dip_int4_gather_down(down_t, scales, n_rows, h, idx, k, out_features, scratch,
+                              sizeof(g_noalloc_partials), y, stream);
+}

@@ -116,6 +116,25 @@ DIP_API int dip_int4_gather_down(const int8_t* down_t, const dip_bf16* scales, i
                          int64_t out_features, void* workspace, size_t workspace_bytes,
                          dip_bf16* y, dip_stream_t stream);
 
+/* ---- allocation-free variant of dip_int4_gather_down ------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they call in (a host framework owns the memory pool, a fixed
+ * memory budget, or an FFI caller with no CUDA allocator): the same
+ * computation and arguments as dip_int4_gather_down, minus the workspace.
+ * The partial sums go to a static device array of the library, sized for
+ * out_features <= 8192 (148 * 8192 fp32 = 4.6 MiB, held on every GPU that
+ * loads the library until the process exits); larger out_features returns
+ * DIP_ERR_UNSUPPORTED.  Nothing is allocated: no cudaMalloc, no cudaFree.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All calls
+ * share the array and it keeps the last call's contents (every call rewrites
+ * what it reads, so nothing has to start at zero); calls that overlap on the
+ * GPU, on any streams, race on it and must be serialised by the caller. */
+DIP_API int dip_int4_gather_down_noalloc(const int8_t* down_t, const dip_bf16* scales,
+                                         int64_t n_rows, const dip_bf16* h, const int32_t* idx,
+                                         int64_t k, int64_t out_features, dip_bf16* y,
+                                         dip_stream_t stream);
+
 /* ---- a13: dual-source gathered GEMV (cache-aware up) ---------------------------
  * out[j] = dot(dequant(src[j]==0 ? res[row[j]] : str[row[j]]), x).  Replaces
  * ca_fused_ops::ca_fused_gemv (kernels/ca_fused/ca_fused_gemv.cu:87-112);
