@@ -48,6 +48,7 @@ int num_sms() {
 
 size_t down_workspace_bytes(int64_t out);
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+constexpr size_t kHistBytes = 32768 * sizeof(unsigned);  // top-k histogram
 
 }  // namespace dip
 
@@ -82,8 +83,8 @@ extern "C" int dip_take_device_error(unsigned int* out) {
 
 extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k < 0) return 0;
-  return align256((size_t)inter * 2) + align256((size_t)k * 4) + align256((size_t)k * 2) +
-         align256(down_workspace_bytes(hidden));
+  return kHistBytes + align256((size_t)inter * 2) + align256((size_t)k * 4) +
+         align256((size_t)k * 2) + align256(down_workspace_bytes(hidden));
 }
 
 extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k, void* workspace,
@@ -95,6 +96,8 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   if (need == 0) return DIP_ERR_ARG;
   if (workspace_bytes < need) return DIP_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  unsigned* hist = reinterpret_cast<unsigned*>(ws);
+  ws += kHistBytes;
   dip_bf16* g = reinterpret_cast<dip_bf16*>(ws);
   ws += align256((size_t)L->inter * 2);
   int32_t* idx = reinterpret_cast<int32_t*>(ws);
@@ -106,9 +109,10 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   if (g_out) g = g_out;
   if (idx_out) idx = idx_out;
 
-  int st = dip_int4_gemv(L->gate_qw, L->gate_sc, x, g, L->inter, L->hidden, 1, stream);
+  int st = gemv_silu_hist(L->gate_qw, L->gate_sc, x, g, L->inter, L->hidden, hist,
+                          (cudaStream_t)stream);
   if (st) return st;
-  st = dip_topk_select(g, L->inter, k, idx, stream);
+  st = topk_from_hist_launch(g, L->inter, k, idx, hist, (cudaStream_t)stream);
   if (st) return st;
   st = dip_gather_up_h(L->up_qw, L->up_sc, L->inter, x, g, idx, k, L->hidden, h, stream);
   if (st) return st;

@@ -46,6 +46,7 @@ struct GemvParams {
   const int32_t* gid;  // EPI_H: channel id of output j
   uint16_t* out;       // [n_out]
   const int32_t* count;  // optional device-side number of outputs (<= n_out)
+  unsigned* hist;        // EPI_SILU: optional 32768-bin histogram of |g| (bf16 bits)
   int n_out;
   int in_features;
 };
@@ -53,6 +54,13 @@ struct GemvParams {
 constexpr int kGemvWarps = 4;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvBatch = 5;  // groups whose loads are in flight per warp
+
+// Counts one output's |g| (15-bit bf16 magnitude) into the top-k histogram;
+// NaN is never counted, matching the top-k's exclusion of NaN.
+__device__ __forceinline__ void hist_count(unsigned* hist, uint16_t o) {
+  const unsigned key = o & 0x7FFFu;
+  if (hist && key <= 0x7F80u) atomicAdd(&hist[key], 1u);
+}
 
 template <int MODE>
 __device__ __forceinline__ bool resolve_row(const GemvParams& p, int j, const uint8_t*& qw,
@@ -214,6 +222,7 @@ gemv_int4_kernel(const GemvParams p) {
         o = f32_to_bf16_bits(v);
       } else if (EPI == EPI_SILU) {
         o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+        hist_count(p.hist, o);
       } else {
         const float u = round_bf16(v);
         const float gv = bf16_bits_to_f32(p.g[p.gid[j]]);
@@ -425,7 +434,10 @@ gemv_ring_kernel(const GemvParams p, unsigned* err) {
         uint16_t o;
         if (!valid) o = 0;
         else if (EPI == EPI_PLAIN) o = f32_to_bf16_bits(v);
-        else if (EPI == EPI_SILU) o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+        else if (EPI == EPI_SILU) {
+          o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+          hist_count(p.hist, o);
+        }
         else o = f32_to_bf16_bits(bf16_bits_to_f32(p.g[p.gid[j]]) * round_bf16(v));
         p.out[j] = o;
       }
@@ -496,6 +508,28 @@ static bool gemv_shape_ok(int64_t in_features) {
   return in_features > 0 && in_features % kGroup == 0 && in_features <= 65536;
 }
 
+}  // namespace dip
+
+namespace dip {
+// Gate GEMV + SiLU that also fills the top-k histogram (used by the fused
+// decode chain; `hist` must be zero on entry, the top-k leaves it zero).
+int gemv_silu_hist(const int8_t* qweight, const uint16_t* scales, const uint16_t* x,
+                   uint16_t* out, int64_t rows, int64_t in_features, unsigned* hist,
+                   cudaStream_t stream) {
+  if (rows <= 0 || rows > INT32_MAX || !gemv_shape_ok(in_features)) return DIP_ERR_ARG;
+  if (!qweight || !scales || !x || !out || !hist || !aligned16(qweight) || !aligned16(x))
+    return DIP_ERR_ARG;
+  GemvParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(qweight);
+  p.sc0 = scales;
+  p.n0 = rows;
+  p.x = x;
+  p.out = out;
+  p.hist = hist;
+  p.n_out = (int)rows;
+  p.in_features = (int)in_features;
+  return launch_gemv<ROW_DENSE, EPI_SILU>(p, stream);
+}
 }  // namespace dip
 
 using namespace dip;

@@ -307,6 +307,121 @@ ca_split_kernel(const int32_t* __restrict__ idx, int k, const int64_t* __restric
   if (tid == 0) n_hit[0] = tot.x;
 }
 
+// ---------------------------------------------------------------------------
+// Histogram-based top-k (the fast path).  The exact bisection emulation needs
+// only w, the (k+1)-th largest |s|, and max|s|; both come from a 32768-bin
+// histogram of the 15-bit magnitudes.  In the fused decode chain the gate
+// kernel fills the histogram in its epilogue (one global atomic per channel),
+// so the select kernel below only scans 128 KB and compacts.  It leaves the
+// histogram zero for the next call.
+constexpr int kHistBins = 32768;
+
+__global__ void __launch_bounds__(256)
+topk_hist_kernel(const uint16_t* __restrict__ s, int n, unsigned* __restrict__ hist) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned key = s[i] & 0x7FFFu;
+    if (key <= 0x7F80u) atomicAdd(&hist[key], 1u);
+  }
+  pdl_launch_dependents();
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __restrict__ idx,
+                      unsigned* __restrict__ hist) {
+  extern __shared__ __align__(16) uint16_t keys[];
+  __shared__ int2 warp_tot[33];
+  __shared__ unsigned s_max;
+  __shared__ unsigned s_w;
+  __shared__ float s_lohi[2];
+  const int tid = threadIdx.x;
+  if (tid == 0) { s_max = 0; s_w = 0; }
+  pdl_wait();
+  // Thread tid owns bins [32 tid, 32 tid + 32): counts, then zero them.
+  uint4* hv = reinterpret_cast<uint4*>(hist) + tid * 8;
+  unsigned c[32];
+  int tot_mine = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint4 v = hv[q];
+    c[4 * q] = v.x; c[4 * q + 1] = v.y; c[4 * q + 2] = v.z; c[4 * q + 3] = v.w;
+    tot_mine += v.x + v.y + v.z + v.w;
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) hv[q] = make_uint4(0, 0, 0, 0);
+  // Stage |s| for the compaction meanwhile.
+  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
+  const int nvec = vec ? n / 8 : 0;
+  for (int v = tid; v < nvec; v += kTopkThreads) {
+    uint4 r = __ldg(reinterpret_cast<const uint4*>(s) + v);
+    r.x &= 0x7FFF7FFFu; r.y &= 0x7FFF7FFFu; r.z &= 0x7FFF7FFFu; r.w &= 0x7FFF7FFFu;
+    reinterpret_cast<uint4*>(keys)[v] = r;
+  }
+  for (int i = nvec * 8 + tid; i < n; i += kTopkThreads) keys[i] = s[i] & 0x7FFF;
+  int2 tot;
+  const int2 pre = block_excl_scan2(tot_mine, 0, warp_tot, tot);  // also a barrier
+  const int nvalid = tot.x;
+  const int above = nvalid - pre.x - tot_mine;  // count in bins above my range
+  if (tot_mine > 0) {
+    int top = 31;
+    while (c[top] == 0) --top;
+    atomicMax(&s_max, (unsigned)(tid * 32 + top));
+  }
+  const bool has_w = nvalid >= k + 1;
+  if (has_w && above < k + 1 && k + 1 <= above + tot_mine) {
+    int run = above;
+    for (int b = 31; b >= 0; --b) {
+      run += c[b];
+      if (run >= k + 1) { s_w = (unsigned)(tid * 32 + b); break; }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const float wv = bf16_bits_to_f32(s_w);
+    float hi = bf16_bits_to_f32(s_max);
+    float lo = 0.0f;
+    float t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    for (int step = 0; step < 25; ++step) {
+      if (has_w && wv > t) lo = t; else hi = t;
+      t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    }
+    s_lohi[0] = lo;
+    s_lohi[1] = hi;
+  }
+  __syncthreads();
+  const float lo = s_lohi[0], hi = s_lohi[1];
+  const int per = (n + kTopkThreads - 1) / kTopkThreads;
+  const int beg = min(n, tid * per), end = min(n, beg + per);
+  int ca = 0, cb = 0;
+  for (int i = beg; i < end; ++i) {
+    const float v = bf16_bits_to_f32(keys[i]);
+    ca += (v > hi);
+    cb += (v > lo && v <= hi);
+  }
+  const int2 off = block_excl_scan2(ca, cb, warp_tot, tot);
+  int pa = off.x, pb = tot.x + off.y;
+  for (int i = beg; i < end; ++i) {
+    const float v = bf16_bits_to_f32(keys[i]);
+    if (v > hi) { if (pa < k) idx[pa] = i; ++pa; }
+    else if (v > lo && v <= hi) { if (pb < k) idx[pb] = i; ++pb; }
+  }
+  pdl_launch_dependents();
+  const int filled = min(k, tot.x + tot.y);
+  for (int i = filled + tid; i < k; i += kTopkThreads) idx[i] = 0;
+}
+
+int topk_from_hist_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx,
+                          unsigned* hist, cudaStream_t st) {
+  if (n < 1 || n > kTopkMaxN || k < 1 || k > INT32_MAX || !s || !idx || !hist) return DIP_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(hist) & 15) != 0) return DIP_ERR_ARG;
+  const size_t smem = (size_t)n * 2;
+  cudaError_t e = cudaFuncSetAttribute(topk_from_hist_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return launch_status(e);
+  return launch_status(launch(topk_from_hist_kernel, dim3(1), dim3(kTopkThreads), smem, st, s,
+                              (int)n, (int)k, idx, hist));
+}
+
 int topk_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, int batch,
                 int64_t s_stride, int64_t idx_stride, cudaStream_t st) {
   if (n < 1 || n > kTopkMaxN || k < 0 || k > INT32_MAX || batch < 1) return DIP_ERR_ARG;
@@ -356,4 +471,18 @@ extern "C" int dip_shard_select(const int32_t* idx, int64_t k, int64_t lo, int64
   return launch_status(launch(shard_select_kernel, dim3(1), dim3(kTopkThreads), 0,
                               (cudaStream_t)stream, idx, (int)k, (int)lo, (int)hi, local_idx,
                               count));
+}
+
+extern "C" size_t dip_topk_hist_bytes(void) { return kHistBins * sizeof(unsigned); }
+
+extern "C" int dip_topk_select_ws(const dip_bf16* s, int64_t n, int64_t k, int32_t* idx,
+                                  void* hist, dip_stream_t stream) {
+  if (n < 1 || n > kTopkMaxN || k < 0 || k > INT32_MAX || !s || !hist) return DIP_ERR_ARG;
+  if (k == 0) return DIP_OK;
+  if (!idx) return DIP_ERR_ARG;
+  const int grid = (int)((n + 255) / 256 < 148 ? (n + 255) / 256 : 148);
+  int st = launch_status(launch(topk_hist_kernel, dim3(grid), dim3(256), 0, (cudaStream_t)stream,
+                                s, (int)n, static_cast<unsigned*>(hist)));
+  if (st) return st;
+  return topk_from_hist_launch(s, n, k, idx, static_cast<unsigned*>(hist), (cudaStream_t)stream);
 }

@@ -84,7 +84,9 @@ Tensor topk_select(const Tensor& s_in, int64_t k) {
   TORCH_CHECK(k >= 0, "topk_select: k must be >= 0");
   Tensor idx = at::empty({k}, s.options().dtype(at::kInt));
   if (k == 0) return idx;
-  check_status(dip_topk_select(bf(s), s.numel(), k, idx.data_ptr<int32_t>(), cur_stream()),
+  Tensor hist = at::zeros({(int64_t)dip_topk_hist_bytes()}, s.options().dtype(at::kByte));
+  check_status(dip_topk_select_ws(bf(s), s.numel(), k, idx.data_ptr<int32_t>(), hist.data_ptr(),
+                                  cur_stream()),
                "topk_select");
   return idx;
 }
@@ -274,7 +276,8 @@ Tensor srcrow_down(const Tensor& res_dt, const Tensor& res_sc, const Tensor& ful
 std::tuple<Tensor, Tensor, Tensor> mlp_decode(const Tensor& gate_qw, const Tensor& gate_sc,
                                               const Tensor& up_qw, const Tensor& up_sc,
                                               const Tensor& dt_qw, const Tensor& dt_sc,
-                                              const Tensor& x_in, int64_t k) {
+                                              const Tensor& x_in, int64_t k,
+                                              const std::optional<Tensor>& ws_opt) {
   check_packed(gate_qw, gate_sc, "mlp_decode(gate)");
   check_packed(up_qw, up_sc, "mlp_decode(up)");
   check_packed(dt_qw, dt_sc, "mlp_decode(down_t)");
@@ -290,7 +293,9 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode(const Tensor& gate_qw, const Tenso
   Tensor y = bf16_empty(hidden, x), g = bf16_empty(inter, x);
   Tensor idx = at::empty({k}, x.options().dtype(at::kInt));
   const size_t wsb = dip_mlp_workspace_bytes(hidden, inter, k);
-  Tensor ws = at::empty({(int64_t)wsb}, x.options().dtype(at::kByte));
+  Tensor ws = ws_opt.has_value() ? *ws_opt : at::zeros({(int64_t)wsb}, x.options().dtype(at::kByte));
+  TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && (size_t)ws.nbytes() >= wsb,
+              "mlp_decode: workspace too small (need ", wsb, " bytes)");
   check_status(dip_mlp_decode(&L, bf(x), k, ws.data_ptr(), wsb, bfm(y), bfm(g),
                               idx.data_ptr<int32_t>(), cur_stream()),
                "mlp_decode");
@@ -403,6 +408,10 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
   return y;
 }
 
+int64_t op_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
+  return (int64_t)dip_mlp_workspace_bytes(hidden, inter, k);
+}
+
 int64_t op_set_pdl(int64_t enable) { return dip_set_pdl((int)enable); }
 int64_t op_set_gemv_variant(int64_t simple) { return dip_set_gemv_variant((int)simple); }
 int64_t op_take_device_error() {
@@ -450,7 +459,8 @@ TORCH_LIBRARY(dip_b200, m) {
       "Tensor src, Tensor row) -> Tensor");
   m.def(
       "mlp_decode(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, Tensor down_t_qw, "
-      "Tensor down_t_sc, Tensor x, int k) -> (Tensor, Tensor, Tensor)");
+      "Tensor down_t_sc, Tensor x, int k, Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
+  m.def("mlp_workspace_bytes(int hidden, int inter, int k) -> int");
   m.def("quantize_int4(Tensor w) -> (Tensor, Tensor)");
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
@@ -485,6 +495,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
 }
 TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) {
   m.impl("set_pdl", &op_set_pdl);
+  m.impl("mlp_workspace_bytes", &op_mlp_workspace_bytes);
   m.impl("set_gemv_variant", &op_set_gemv_variant);
   m.impl("take_device_error", &op_take_device_error);
 }

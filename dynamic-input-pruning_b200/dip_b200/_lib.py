@@ -94,7 +94,7 @@ def _register_fakes() -> None:
         return torch.empty(dt_qw.shape[1] * 2, dtype=torch.bfloat16, device=h.device)
 
     @rf("dip_b200::mlp_decode")
-    def _(gq, gs, uq, us, dq, ds, x, k):
+    def _(gq, gs, uq, us, dq, ds, x, k, workspace=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))

@@ -93,6 +93,10 @@ class DipStack:
         """x0 [hidden] bf16, resid [n_layers, hidden] bf16 -> last layer's y."""
         x = x0
         k = self.cfg.k
+        if getattr(self, "_ws", None) is None or self._ws.device != x0.device:
+            nb = torch.ops.dip_b200.mlp_workspace_bytes(self.cfg.hidden, self.cfg.inter, k)
+            # zeroed once; every decode call leaves the histogram region zero
+            self._ws = torch.zeros(nb, dtype=torch.uint8, device=x0.device)
         idxs = []
         y = None
         for l, L in enumerate(self.layers):
@@ -100,7 +104,7 @@ class DipStack:
                 x = torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
             y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"], L["up_qw"],
                                                       L["up_sc"], L["down_t_qw"],
-                                                      L["down_t_sc"], x, k)
+                                                      L["down_t_sc"], x, k, self._ws)
             if record:
                 idxs.append(idx)
         if record:

@@ -87,6 +87,15 @@ DIP_API int dip_topk_select(const dip_bf16* s, int64_t n, int64_t k, int32_t* id
 DIP_API int dip_topk_select_batched(const dip_bf16* s, int64_t batch, int64_t n, int64_t s_stride,
                             int64_t k, int32_t* idx, int64_t idx_stride, dip_stream_t stream);
 
+/* Faster form of dip_topk_select (same indices): a histogram pass plus a
+ * select/compaction pass over a caller-provided histogram of
+ * dip_topk_hist_bytes() bytes (16-byte aligned) that must be ZERO on entry;
+ * the call leaves it zero again, so one buffer serves any number of calls on
+ * one stream. */
+DIP_API size_t dip_topk_hist_bytes(void);
+DIP_API int dip_topk_select_ws(const dip_bf16* s, int64_t n, int64_t k, int32_t* idx, void* hist,
+                               dip_stream_t stream);
+
 /* ---- a8: gathered int4 GEMV --------------------------------------------------
  * out[j] = bf16(dot(dequant(W[indices[j]]), x)), j < k.  Replaces
  * int4_gather_ops::int4_gather_gemv (kernels/int4_gather/int4_gather_gemv.cu:
@@ -182,6 +191,14 @@ typedef struct dip_layer {
 } dip_layer_t;
 
 DIP_API size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k);
+/* The workspace must be ZERO before its first use (its first 128 KB hold the
+ * top-k histogram, which the gate kernel fills and the top-k clears); every
+ * call leaves that region zero, so a workspace can be reused call after call
+ * on one stream. */
+/* The workspace must be ZERO before its first use (its first 128 KB hold the
+ * top-k histogram, which the gate kernel fills and the top-k clears); every
+ * call leaves that region zero, so a workspace can be reused call after call
+ * on one stream. */
 /* g_out (bf16[inter]) and idx_out (int32[k]) may be NULL; when given they
  * receive the layer's gate activations and selected channels. */
 DIP_API int dip_mlp_decode(const dip_layer_t* layer, const dip_bf16* x, int64_t k, void* workspace,
