@@ -48,7 +48,7 @@ int num_sms() {
 
 size_t down_workspace_bytes(int64_t out);
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-constexpr size_t kHistBytes = 32768 * sizeof(unsigned);  // top-k histogram
+
 
 }  // namespace dip
 
@@ -83,7 +83,7 @@ extern "C" int dip_take_device_error(unsigned int* out) {
 
 extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k < 0) return 0;
-  return kHistBytes + align256((size_t)inter * 2) + align256((size_t)k * 4) +
+  return align256(topk_scratch_bytes()) + align256((size_t)inter * 2) + align256((size_t)k * 4) +
          align256((size_t)k * 2) + align256(down_workspace_bytes(hidden));
 }
 
@@ -97,7 +97,7 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   if (workspace_bytes < need) return DIP_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   unsigned* hist = reinterpret_cast<unsigned*>(ws);
-  ws += kHistBytes;
+  ws += align256(topk_scratch_bytes());
   dip_bf16* g = reinterpret_cast<dip_bf16*>(ws);
   ws += align256((size_t)L->inter * 2);
   int32_t* idx = reinterpret_cast<int32_t*>(ws);
@@ -112,10 +112,10 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   int st = gemv_silu_hist(L->gate_qw, L->gate_sc, x, g, L->inter, L->hidden, hist,
                           (cudaStream_t)stream);
   if (st) return st;
-  st = topk_from_hist_launch(g, L->inter, k, idx, hist, (cudaStream_t)stream);
+  st = topk_compact_launch(g, L->inter, k, idx, hist, (cudaStream_t)stream);
   if (st) return st;
   st = dip_gather_up_h(L->up_qw, L->up_sc, L->inter, x, g, idx, k, L->hidden, h, stream);
   if (st) return st;
-  return dip_int4_gather_down(L->down_t_qw, L->down_t_sc, L->inter, h, idx, k, L->hidden, part,
-                              part_bytes, y, stream);
+  return gather_down_clear(L->down_t_qw, L->down_t_sc, L->inter, h, idx, k, L->hidden, part,
+                           part_bytes, y, hist, topk_scratch_bytes(), (cudaStream_t)stream);
 }

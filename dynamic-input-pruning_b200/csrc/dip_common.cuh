@@ -132,6 +132,17 @@ int gemv_silu_hist(const int8_t* qweight, const uint16_t* scales, const uint16_t
                    cudaStream_t stream);
 int topk_from_hist_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx,
                           unsigned* hist, cudaStream_t st);
+// Top-k scratch: fine histogram [32768], coarse histogram [256], look-back words.
+constexpr int kTopkHistBins = 32768;
+size_t topk_scratch_bytes();
+int topk_compact_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, unsigned* scratch,
+                        cudaStream_t st);
+// Gathered down projection that also clears `clear_bytes` of `clear` (16-byte
+// multiple) in its reduction kernel.
+int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_rows,
+                      const uint16_t* h, const int32_t* idx, int64_t k, int64_t out_features,
+                      void* workspace, size_t workspace_bytes, uint16_t* y, void* clear,
+                      size_t clear_bytes, cudaStream_t stream);
 
 }  // namespace dip
 

@@ -32,6 +32,8 @@ struct DownParams {
   const int32_t* row;     // SRCROW
   float* partial;         // [gridDim.x, out]
   const int32_t* count;   // optional device-side number of rows (<= k)
+  uint4* clear;           // optional: zeroed by the reduction kernel
+  int clear_n16;
   int k;
   int out_features;
 };
@@ -152,11 +154,14 @@ gather_down_kernel(const DownParams p) {
 // grid = out/32 CTAs of 256 threads: warp w sums partials w, w+8, ...
 __global__ void __launch_bounds__(256)
 reduce_partials_kernel(const float* __restrict__ partial, int nparts, int out,
-                       uint16_t* __restrict__ y, float* __restrict__ y_f32) {
+                       uint16_t* __restrict__ y, float* __restrict__ y_f32,
+                       uint4* __restrict__ clear, int clear_n16) {
   __shared__ float red[8][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int o = blockIdx.x * 32 + lane;
   pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < clear_n16; i += gridDim.x * blockDim.x)
+    clear[i] = make_uint4(0, 0, 0, 0);
   float v = 0.f;
   if (o < out) {
 #pragma unroll 4
@@ -189,115 +194,117 @@ reduce_partials_kernel(const float* __restrict__ partial, int nparts, int out,
 // end).  The tensor core therefore does both the multiply-adds and the
 // channel reduction; a lane spends ~1.2 instructions per weight nibble.
 //
-// Grid: 2 output halves x S channel slices.  Each CTA streams, for its
-// slice, the half rows (out/4 bytes) plus the scale row of 16 channels per
-// stage into an 8-stage shared-memory ring with cp.async.bulk (producer warp)
-// and has out/256 consumer warps, warp w owning output group w of the half
-// (64 bytes of every row, 8 accumulator m-tiles = 32 fp32 registers).
-constexpr int kDmStages = 8;
-constexpr int kDmChan = 16;       // channels per stage (one MMA K step)
+// Grid: 2 output halves x S channel slices.  A CTA has out/256 warps; warp w
+// owns output group w of its half (64 bytes of every selected row, 8
+// accumulator m-tiles = 32 fp32 registers) and streams its own bytes with
+// asynchronous 16-byte copies (cp.async.cg; the warp's 64 bytes of 16 rows
+// are 64 chunks, two per lane) plus the 4-byte scale pairs through a private
+// 6-tile shared-memory pipeline, so no block-level synchronisation is needed
+// after the prologue.  (16-byte .cg copies measured 6.7 TB/s on B200 in this
+// access pattern; .ca copies 4.2 TB/s.)
+constexpr int kDmChan = 16;       // channels per tile (one MMA K step)
 constexpr int kDmSlices = 74;     // channel slices; 2 x 74 = 148 CTAs
-constexpr int kDmPad = 16;
+constexpr int kDmDepth = 6;       // tiles in flight per warp
+constexpr int kDmRowPitch = 80;   // 64 bytes of a row + pad (conflict-free 8-byte reads)
+constexpr int kDmSlotW = kDmChan * kDmRowPitch;
+constexpr int kDmSlotBytes = kDmSlotW + kDmChan * 4;  // weights + scale pairs
+
+__device__ __forceinline__ void cp_async16g(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_d() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_depth() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kDmDepth - 1) : "memory");
+}
 
 struct DmGeom {
-  int half_bytes, row_stride, scb, stage_bytes, h_off, bar_off, total;
+  int ring_off, rows_off, h_off, total;
 };
-__host__ __device__ inline DmGeom dm_geom(int out, int max_slice) {
+__host__ __device__ inline DmGeom dm_geom(int nwarps, int max_slice) {
   DmGeom g;
-  g.half_bytes = out / 4;
-  g.row_stride = g.half_bytes + kDmPad;
-  g.scb = (out / kGroup) * 2;
-  g.stage_bytes = (kDmChan * g.row_stride + kDmChan * g.scb + 127) & ~127;
-  g.h_off = kDmStages * g.stage_bytes;
-  g.bar_off = g.h_off + ((max_slice * 4 + 15) & ~15);
-  g.total = g.bar_off + 2 * kDmStages * 8;
+  g.ring_off = 0;
+  g.rows_off = nwarps * kDmDepth * kDmSlotBytes;
+  g.h_off = g.rows_off + max_slice * 16;  // two pointers per channel
+  g.total = g.h_off + max_slice * 4;
   return g;
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(672, 1)
-down_mma_kernel(const DownParams p, int max_slice, unsigned* err) {
+__global__ void __launch_bounds__(640, 1)
+down_mma_kernel(const DownParams p, int max_slice) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int out = p.out_features;
-  const int nwarps = out / 256;  // consumer warps
-  const DmGeom geo = dm_geom(out, max_slice);
-  float* hsm = reinterpret_cast<float*>(smem + geo.h_off);  // h of the slice (fp32)
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + geo.bar_off);
-  uint64_t* empty = full + kDmStages;
+  const int nwarps = out / 256;
+  const DmGeom geo = dm_geom(nwarps, max_slice);
+  const uint8_t** rowq = reinterpret_cast<const uint8_t**>(smem + geo.rows_off);
+  const uint16_t** rows_sc = reinterpret_cast<const uint16_t**>(smem + geo.rows_off) + max_slice;
+  float* hsm = reinterpret_cast<float*>(smem + geo.h_off);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = blockIdx.x & 1, slice = blockIdx.x >> 1, nslices = gridDim.x >> 1;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kDmStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], nwarps);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
   pdl_wait();
   int k = p.k;
   if (p.count) k = min(k, *p.count);
   const int j0 = (int)((int64_t)k * slice / nslices);
   const int j1 = (int)((int64_t)k * (slice + 1) / nslices);
-  const int nstage = (j1 - j0 + kDmChan - 1) / kDmChan;
-
-  if (warp == nwarps) {
-    // ---------------- producer ----------------
-    bool ok = true;
-    for (int i = 0; i < nstage && ok; ++i) {
-      const int s = i % kDmStages;
-      if (lane == 0) ok = mbar_wait(&empty[s], ((i / kDmStages) & 1) ^ 1, err);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const int c0 = j0 + i * kDmChan;
-      const int rows = min(kDmChan, j1 - c0);
-      uint8_t* st = smem + s * geo.stage_bytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], rows * (geo.half_bytes + geo.scb));
-      __syncwarp();
-      if (lane < rows) {
-        const uint8_t* qw;
-        const uint16_t* sc;
-        down_row<MODE>(p, c0 + lane, qw, sc);
-        bulk_g2s(st + lane * geo.row_stride, qw + half * geo.half_bytes, geo.half_bytes,
-                 &full[s]);
-        bulk_g2s(st + kDmChan * geo.row_stride + lane * geo.scb, sc, geo.scb, &full[s]);
-      }
-    }
-    if (lane == 0 && ok) {
-      for (int i = max(0, nstage - kDmStages); i < nstage; ++i)
-        if (!mbar_wait(&full[i % kDmStages], (i / kDmStages) & 1, err)) break;
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  // h of this slice (0 for channels whose row index is out of range).
-  for (int j = j0 + threadIdx.x; j < j1; j += nwarps * 32) {
+  const int nrow = j1 - j0;
+  for (int j = threadIdx.x; j < nrow; j += blockDim.x) {
     const uint8_t* qw;
     const uint16_t* sc;
-    const bool okr = down_row<MODE>(p, j, qw, sc);
-    hsm[j - j0] = okr ? bf16_bits_to_f32(p.h[j]) : 0.f;
+    const bool okr = down_row<MODE>(p, j0 + j, qw, sc);
+    rowq[j] = qw;
+    rows_sc[j] = sc;
+    hsm[j] = okr ? bf16_bits_to_f32(p.h[j0 + j]) : 0.f;
   }
-  named_bar(1, nwarps * 32);
+  __syncthreads();
 
   const int gq = lane >> 2, tq = lane & 3;
   const int og = half * nwarps + warp;  // global output group of this warp
-  // Table lane mapping: lanes 0..15 -> (pair = lane & 7, which = lane >> 3).
+  const int seg_off = half * (out / 4) + warp * 64;  // this warp's 64 bytes of a row
+  uint8_t* ring = smem + geo.ring_off + warp * kDmDepth * kDmSlotBytes;
+  const int ntile = (nrow + kDmChan - 1) / kDmChan;
+
+  auto issue = [&](int i) {
+    if (i < ntile) {
+      uint8_t* slot = ring + (i % kDmDepth) * kDmSlotBytes;
+      const int c0 = i * kDmChan;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int ch = lane + 32 * h2;  // 64 chunks: row ch/4, 16-byte part ch%4
+        const int r = ch >> 2, part = ch & 3;
+        const int c = min(c0 + r, nrow - 1);
+        cp_async16g(slot + r * kDmRowPitch + part * 16, rowq[c] + seg_off + part * 16);
+      }
+      if (lane < kDmChan) {
+        const int c = min(c0 + lane, nrow - 1);
+        cp_async4(slot + kDmSlotW + lane * 4, rows_sc[c] + (og & ~1));
+      }
+    }
+    cp_async_commit_d();
+  };
+#pragma unroll
+  for (int i = 0; i < kDmDepth - 1; ++i) issue(i);
+
   const int tpair = lane & 7, twhich = (lane >> 3) & 1;
   float acc[8][4];
 #pragma unroll
   for (int m = 0; m < 8; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
   float colsum = 0.f;
-  bool ok = true;
-  for (int i = 0; i < nstage; ++i) {
-    const int s = i % kDmStages;
-    if (ok) ok = mbar_wait(&full[s], (i / kDmStages) & 1, err);
-    const uint8_t* st = smem + s * geo.stage_bytes;
-    const int c0 = i * kDmChan;  // slice-local channel of row 0
-    const int rows = min(kDmChan, j1 - j0 - c0);
-    // B values: lane (pair, which) packs channels 2*pair, 2*pair+1 of this
-    // stage as bf16x2 of hi (which 0) or lo (which 1) of h*s.
+  for (int i = 0; i < ntile; ++i) {
+    issue(i + kDmDepth - 1);
+    cp_async_wait_depth();
+    __syncwarp();
+    const uint8_t* slot = ring + (i % kDmDepth) * kDmSlotBytes;
+    const int c0 = i * kDmChan;
+    // B values: lane (pair, which) packs channels 2*pair, 2*pair+1 as bf16x2
+    // of hi (which 0) or lo (which 1) of h*s.
     uint32_t bval = 0;
     if (lane < 16) {
       float v2[2];
@@ -305,10 +312,9 @@ down_mma_kernel(const DownParams p, int max_slice, unsigned* err) {
       for (int e = 0; e < 2; ++e) {
         const int c = 2 * tpair + e;
         float hs = 0.f;
-        if (c < rows) {
-          const uint16_t* sc =
-              reinterpret_cast<const uint16_t*>(st + kDmChan * geo.row_stride + c * geo.scb);
-          hs = hsm[c0 + c] * bf16_bits_to_f32(sc[og]);
+        if (c0 + c < nrow) {
+          const uint16_t* scp = reinterpret_cast<const uint16_t*>(slot + kDmSlotW + c * 4);
+          hs = hsm[c0 + c] * bf16_bits_to_f32(scp[og & 1]);
         }
         const float hi = round_bf16(hs);
         v2[e] = twhich ? round_bf16(hs - hi) : hi;
@@ -319,32 +325,29 @@ down_mma_kernel(const DownParams p, int max_slice, unsigned* err) {
     const int src = (gq & 1) * 8;
     const uint32_t b0 = __shfl_sync(0xffffffffu, bval, src + tq);
     const uint32_t b1 = __shfl_sync(0xffffffffu, bval, src + tq + 4);
-    if (ok) {
-      // rows 2t, 2t+1, 2t+8, 2t+9 of the stage, bytes [64*warp + 8*g, +8)
-      const int boff = warp * 64 + gq * 8;
-      const uint2 ra = *reinterpret_cast<const uint2*>(st + (2 * tq) * geo.row_stride + boff);
-      const uint2 rb = *reinterpret_cast<const uint2*>(st + (2 * tq + 1) * geo.row_stride + boff);
-      const uint2 rc = *reinterpret_cast<const uint2*>(st + (2 * tq + 8) * geo.row_stride + boff);
-      const uint2 rd = *reinterpret_cast<const uint2*>(st + (2 * tq + 9) * geo.row_stride + boff);
-      const uint32_t pab[4] = {__byte_perm(ra.x, rb.x, 0x5410), __byte_perm(ra.x, rb.x, 0x7632),
-                               __byte_perm(ra.y, rb.y, 0x5410), __byte_perm(ra.y, rb.y, 0x7632)};
-      const uint32_t pcd[4] = {__byte_perm(rc.x, rd.x, 0x5410), __byte_perm(rc.x, rd.x, 0x7632),
-                               __byte_perm(rc.y, rd.y, 0x5410), __byte_perm(rc.y, rd.y, 0x7632)};
+    // rows 2t, 2t+1, 2t+8, 2t+9 of the tile, bytes [8g, 8g+8) of the segment
+    const uint2 ra = *reinterpret_cast<const uint2*>(slot + (2 * tq) * kDmRowPitch + gq * 8);
+    const uint2 rb = *reinterpret_cast<const uint2*>(slot + (2 * tq + 1) * kDmRowPitch + gq * 8);
+    const uint2 rc = *reinterpret_cast<const uint2*>(slot + (2 * tq + 8) * kDmRowPitch + gq * 8);
+    const uint2 rd = *reinterpret_cast<const uint2*>(slot + (2 * tq + 9) * kDmRowPitch + gq * 8);
+    const uint32_t pab[4] = {__byte_perm(ra.x, rb.x, 0x5410), __byte_perm(ra.x, rb.x, 0x7632),
+                             __byte_perm(ra.y, rb.y, 0x5410), __byte_perm(ra.y, rb.y, 0x7632)};
+    const uint32_t pcd[4] = {__byte_perm(rc.x, rd.x, 0x5410), __byte_perm(rc.x, rd.x, 0x7632),
+                             __byte_perm(rc.y, rd.y, 0x5410), __byte_perm(rc.y, rd.y, 0x7632)};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t xa[4], xc[4];
-        nib8_biased_bf16x2(pab[q], xa);
-        nib8_biased_bf16x2(pcd[q], xc);
-        // m-tile 2q: byte 2q of the lane's 8 (low nibble -> row g, high -> g+8)
-        const uint32_t a0[4] = {xa[0], xa[1], xc[0], xc[1]};
-        const uint32_t a1[4] = {xa[2], xa[3], xc[2], xc[3]};
-        mma_bf16_16816(acc[2 * q], a0, b0, b1);
-        mma_bf16_16816(acc[2 * q + 1], a1, b0, b1);
-      }
+    for (int q = 0; q < 4; ++q) {
+      uint32_t xa[4], xc[4];
+      nib8_biased_bf16x2(pab[q], xa);
+      nib8_biased_bf16x2(pcd[q], xc);
+      // m-tile 2q+e: byte 2q+e of the lane's 8 (low nibble -> row g, high -> g+8)
+      const uint32_t a0[4] = {xa[0], xa[1], xc[0], xc[1]};
+      const uint32_t a1[4] = {xa[2], xa[3], xc[2], xc[3]};
+      mma_bf16_16816(acc[2 * q], a0, b0, b1);
+      mma_bf16_16816(acc[2 * q + 1], a1, b0, b1);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    __syncwarp();  // the slot is refilled by the next iteration's copies
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   pdl_launch_dependents();
   // Column sums of hi (lanes 0..7) and lo (lanes 8..15) -> their total.
 #pragma unroll
@@ -357,8 +360,8 @@ down_mma_kernel(const DownParams p, int max_slice, unsigned* err) {
     float v[16];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-      v[2 * m] = ok ? acc[m][0] + acc[m][1] - bias : 0.f;
-      v[2 * m + 1] = ok ? acc[m][2] + acc[m][3] - bias : 0.f;
+      v[2 * m] = acc[m][0] + acc[m][1] - bias;
+      v[2 * m + 1] = acc[m][2] + acc[m][3] - bias;
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q)
@@ -388,19 +391,18 @@ int launch_down(DownParams p, uint16_t* y, float* y_f32, void* ws, size_t ws_byt
   if (dm_ok(p) && !force_simple_gemv() && p.k > 0) {
     const int nsl = p.k < kDmSlices ? p.k : kDmSlices;
     const int max_slice = (p.k + nsl - 1) / nsl + 1;
-    const DmGeom geo = dm_geom(out, max_slice);
+    const DmGeom geo = dm_geom(out / 256, max_slice);
     if (geo.total <= 220 * 1024) {
       auto kern = down_mma_kernel<MODE>;
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            geo.total);
       if (e != cudaSuccess) return launch_status(e);
-      unsigned* err = error_word_ptr();
-      if (!err) return DIP_ERR_CUDA;
-      int st1 = launch_status(launch(kern, dim3(2 * nsl), dim3((out / 256 + 1) * 32),
-                                     (size_t)geo.total, st, p, max_slice, err));
+      int st1 = launch_status(launch(kern, dim3(2 * nsl), dim3(out / 256 * 32), (size_t)geo.total,
+                                     st, p, max_slice));
       if (st1 != DIP_OK) return st1;
       return launch_status(launch(reduce_partials_kernel, dim3((out + 31) / 32), dim3(256), 0,
-                                  st, (const float*)p.partial, nsl, out, y, y_f32));
+                                  st, (const float*)p.partial, nsl, out, y, y_f32, p.clear,
+                                  p.clear_n16));
     }
   }
   const int nch = out / 32;
@@ -417,7 +419,8 @@ int launch_down(DownParams p, uint16_t* y, float* y_f32, void* ws, size_t ws_byt
   int st1 = launch_status(launch(kern, dim3(nparts), dim3(teams * nch), smem, st, p));
   if (st1 != DIP_OK) return st1;
   return launch_status(launch(reduce_partials_kernel, dim3((out + 31) / 32), dim3(256), 0, st,
-                              (const float*)p.partial, nparts, out, y, y_f32));
+                              (const float*)p.partial, nparts, out, y, y_f32, p.clear,
+                              p.clear_n16));
 }
 
 template int launch_down<DROW_IDENT>(DownParams, uint16_t*, float*, void*, size_t, cudaStream_t);
@@ -457,7 +460,7 @@ extern "C" int dip_int4_gather_down(const int8_t* down_t, const dip_bf16* scales
     if (e != cudaSuccess) return launch_status(e);
     return launch_status(launch(reduce_partials_kernel, dim3((out_features + 31) / 32), dim3(256),
                                 0, (cudaStream_t)stream, (const float*)workspace, 1,
-                                (int)out_features, y, (float*)nullptr));
+                                (int)out_features, y, (float*)nullptr, (uint4*)nullptr, 0));
   }
   if (idx) return launch_down<DROW_GATHER>(p, y, nullptr, workspace, workspace_bytes,
                                            (cudaStream_t)stream);
@@ -551,3 +554,25 @@ extern "C" int dip_int4_gather_down_noalloc(const int8_t* down_t, const dip_bf16
   return dip_int4_gather_down(down_t, scales, n_rows, h, idx, k, out_features, scratch,
                               sizeof(g_noalloc_partials), y, stream);
 }
+
+namespace dip {
+int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_rows,
+                      const uint16_t* h, const int32_t* idx, int64_t k, int64_t out_features,
+                      void* workspace, size_t workspace_bytes, uint16_t* y, void* clear,
+                      size_t clear_bytes, cudaStream_t stream) {
+  if (k <= 0 || k > INT32_MAX || n_rows <= 0 || !down_shape_ok(out_features) || !y || !down_t ||
+      !scales || !h || !idx || !al16(down_t) || (clear_bytes % 16) != 0)
+    return DIP_ERR_ARG;
+  DownParams p = {};
+  p.qw0 = reinterpret_cast<const uint8_t*>(down_t);
+  p.sc0 = scales;
+  p.n0 = n_rows;
+  p.h = h;
+  p.idx = idx;
+  p.clear = static_cast<uint4*>(clear);
+  p.clear_n16 = (int)(clear_bytes / 16);
+  p.k = (int)k;
+  p.out_features = (int)out_features;
+  return launch_down<DROW_GATHER>(p, y, nullptr, workspace, workspace_bytes, stream);
+}
+}  // namespace dip

@@ -59,7 +59,10 @@ constexpr int kGemvBatch = 5;  // groups whose loads are in flight per warp
 // NaN is never counted, matching the top-k's exclusion of NaN.
 __device__ __forceinline__ void hist_count(unsigned* hist, uint16_t o) {
   const unsigned key = o & 0x7FFFu;
-  if (hist && key <= 0x7F80u) atomicAdd(&hist[key], 1u);
+  if (hist && key <= 0x7F80u) {
+    atomicAdd(&hist[key], 1u);
+    atomicAdd(&hist[kTopkHistBins + (key >> 7)], 1u);
+  }
 }
 
 template <int MODE>
@@ -233,40 +236,6 @@ gemv_int4_kernel(const GemvParams p) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// Persistent ring variant (used when in_features % 1024 == 0 and the ring
-// fits in shared memory).  One CTA per SM: warp 8 is the producer, streaming
-// 16-row tiles (every row as one bulk copy, plus its scales) into a 4-stage
-// shared-memory ring with cp.async.bulk + mbarrier completion; warps 0..7
-// consume, each owning a fixed K-slice of GW groups whose x fragments stay in
-// registers for the whole kernel.  Rows are stored with a 16-byte pad so the
-// 128-bit shared loads of rows g and g+8 fall in different banks.  In the
-// dense mode the producer issues its first copies before waiting on the
-// predecessor kernel (weights are static), overlapping the previous launch.
-constexpr int kRingConsumers = 8;
-constexpr int kRingThreads = (kRingConsumers + 1) * 32;
-constexpr int kRingStages = 4;
-constexpr int kRingPad = 16;
-
-struct RingGeom {
-  int rowb, scb, row_stride, stage_bytes, x_off, gsum_off, red_off, bar_off, total;
-};
-__host__ __device__ inline RingGeom ring_geom(int in) {
-  RingGeom g;
-  const int G = in / kGroup;
-  g.rowb = in / 2;
-  g.scb = G * 2;
-  g.row_stride = g.rowb + kRingPad;
-  g.stage_bytes = 16 * g.row_stride + 16 * g.scb;
-  g.stage_bytes = (g.stage_bytes + 127) & ~127;
-  g.x_off = kRingStages * g.stage_bytes;
-  g.gsum_off = g.x_off + in * 2;
-  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
-  g.bar_off = g.red_off + 2 * kRingConsumers * 16 * 4;
-  g.total = g.bar_off + 2 * kRingStages * 8;
-  return g;
-}
-
 __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb, const uint32_t* bw,
                                           float (&d0)[4], float (&d1)[4]) {
   const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w};
@@ -283,75 +252,104 @@ __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb, cons
   }
 }
 
-template <int MODE, int EPI, int GW>
-__global__ void __launch_bounds__(kRingThreads, 1)
-gemv_ring_kernel(const GemvParams p, unsigned* err) {
-  extern __shared__ __align__(128) uint8_t smem[];
+// ---------------------------------------------------------------------------
+// Default variant: the same tile / fragment layout as gemv_int4_kernel, but
+// every weight byte a warp needs is requested up front with per-thread
+// asynchronous copies (cp.async, 16 B each) into a warp-private shared-memory
+// area, one commit group per quantisation group.  The warp then consumes the
+// groups in order with cp.async.wait_group, so all of a CTA's loads are in
+// flight at once without holding registers, and several CTAs per SM keep
+// ~150 KB per SM in flight.  A lane reads back only what it copied itself,
+// so no block barrier is needed between the copies and the math.  (A
+// producer-warp ring of 1-D bulk copies was measured slower on B200 for
+// rows of 1.3-2.6 KB: it saturated at 1.7-4.2 TB/s against 6.25 TB/s for
+// per-thread loads.)
+constexpr int kCpaMaxGroupsPerWarp = 16;  // in_features <= 8192
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+// Waits until at most n committed groups of this thread are still pending.
+__device__ __forceinline__ void cp_async_wait(int n) {
+  switch (n) {
+#define DIP_WAIT_CASE(N) case N: asm volatile("cp.async.wait_group " #N ";\n" ::: "memory"); break;
+    DIP_WAIT_CASE(0) DIP_WAIT_CASE(1) DIP_WAIT_CASE(2) DIP_WAIT_CASE(3) DIP_WAIT_CASE(4)
+    DIP_WAIT_CASE(5) DIP_WAIT_CASE(6) DIP_WAIT_CASE(7) DIP_WAIT_CASE(8) DIP_WAIT_CASE(9)
+    DIP_WAIT_CASE(10) DIP_WAIT_CASE(11) DIP_WAIT_CASE(12) DIP_WAIT_CASE(13) DIP_WAIT_CASE(14)
+    default: asm volatile("cp.async.wait_group 15;\n" ::: "memory"); break;
+#undef DIP_WAIT_CASE
+  }
+}
+
+// x staging layout: group g occupies 72 words; lane quad t's 16 words start
+// at word 16 t + 4 (t >> 1), which puts the four quads in distinct banks.
+__device__ __forceinline__ int xperm_word(int grp, int t) { return grp * 72 + t * 16 + (t >> 1) * 4; }
+
+struct CpaGeom {
+  int ngw, warp_bytes, x_off, gsum_off, red_off, total;
+};
+__host__ __device__ inline CpaGeom cpa_geom(int in) {
+  CpaGeom g;
+  const int G = in / kGroup;
+  g.ngw = (G + kGemvWarps - 1) / kGemvWarps;
+  g.warp_bytes = g.ngw * 2 * 32 * 16;
+  g.x_off = kGemvWarps * g.warp_bytes;
+  g.gsum_off = g.x_off + G * 72 * 4;
+  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
+  g.total = g.red_off + kGemvWarps * 16 * 4;
+  return g;
+}
+
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_cpa_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
   const int in = p.in_features;
   const int G = in / kGroup;
-  const RingGeom geo = ring_geom(in);
-  uint32_t* xstage = reinterpret_cast<uint32_t*>(smem + geo.x_off);
+  const CpaGeom geo = cpa_geom(in);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int tile0 = blockIdx.x * 16;
+  uint8_t* wbuf = smem + warp * geo.warp_bytes;  // [u][row a/b][lane] x 16 B
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + geo.x_off);
   float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
   float* red = reinterpret_cast<float*>(smem + geo.red_off);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + geo.bar_off);
-  uint64_t* empty = full + kRingStages;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kRingStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
 
   if (MODE != ROW_DENSE) pdl_wait();
   int n_out = p.n_out;
   if (p.count) n_out = min(n_out, *p.count);
-  const int nt = (n_out + 15) / 16;
-  const int t0 = (int)((int64_t)nt * blockIdx.x / gridDim.x);
-  const int t1 = (int)((int64_t)nt * (blockIdx.x + 1) / gridDim.x);
-  const int ntile = t1 - t0;
+  if (tile0 >= n_out) return;
+  const int ja = min(tile0 + gq, n_out - 1);
+  const int jb = min(tile0 + gq + 8, n_out - 1);
+  const uint8_t *qa, *qb;
+  const uint16_t *sa_p, *sb_p;
+  const bool oka = resolve_row<MODE>(p, ja, qa, sa_p);
+  const bool okb = resolve_row<MODE>(p, jb, qb, sb_p);
 
-  if (warp == kRingConsumers) {
-    // ---------------- producer ----------------
-    bool ok = true;
-    for (int i = 0; i < ntile && ok; ++i) {
-      const int s = i % kRingStages;
-      const uint32_t par = ((i / kRingStages) & 1) ^ 1;
-      if (lane == 0) ok = mbar_wait(&empty[s], par, err);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const int r0 = (t0 + i) * 16;
-      const int rows = min(16, n_out - r0);
-      uint8_t* st = smem + s * geo.stage_bytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], rows * (geo.rowb + geo.scb));
-      __syncwarp();
-      if (lane < rows) {
-        const uint8_t* qw;
-        const uint16_t* sc;
-        resolve_row<MODE>(p, r0 + lane, qw, sc);
-        bulk_g2s(st + lane * geo.row_stride, qw, geo.rowb, &full[s]);
-        bulk_g2s(st + 16 * geo.row_stride + lane * geo.scb, sc, geo.scb, &full[s]);
-      }
+  // All of this warp's weights in flight: groups warp, warp+4, ... (u-th).
+  const int ng = (G - warp + kGemvWarps - 1) / kGemvWarps;  // groups of this warp
+  float sca[kCpaMaxGroupsPerWarp], scb[kCpaMaxGroupsPerWarp];
+#pragma unroll
+  for (int u = 0; u < kCpaMaxGroupsPerWarp; ++u) {
+    if (u < ng) {
+      const int grp = warp + kGemvWarps * u;
+      const int off = grp * kGroupBytes + tq * 16;
+      cp_async16(wbuf + (u * 2 + 0) * 512 + lane * 16, qa + off);
+      cp_async16(wbuf + (u * 2 + 1) * 512 + lane * 16, qb + off);
+      cp_async_commit();
+      sca[u] = bf16_bits_to_f32(ldg_u16(sa_p + grp));
+      scb[u] = bf16_bits_to_f32(ldg_u16(sb_p + grp));
     }
-    // Do not leave with copies in flight: wait (bounded) for the last stages.
-    if (lane == 0 && ok) {
-      for (int i = max(0, ntile - kRingStages); i < ntile; ++i)
-        if (!mbar_wait(&full[i % kRingStages], (i / kRingStages) & 1, err)) break;
-    }
-    return;
   }
-
-  // ---------------- consumers ----------------
-  const int ctid = threadIdx.x;  // 0..255
-  const int gq = lane >> 2, tq = lane & 3;
   if (MODE == ROW_DENSE) pdl_wait();
   {
     const int nwords = in / 8;
     const uint4* xv = reinterpret_cast<const uint4*>(p.x);
-    for (int wi = ctid; wi < ((nwords + 255) & ~255); wi += kRingConsumers * 32) {
+    for (int wi = threadIdx.x; wi < ((nwords + 127) & ~127); wi += kGemvThreads) {
       float part = 0.f;
       if (wi < nwords) {
         const uint4 v = __ldg(xv + wi);
@@ -360,7 +358,8 @@ gemv_ring_kernel(const GemvParams p, unsigned* err) {
         o.y = __byte_perm(v.x, v.z, 0x7632);
         o.z = __byte_perm(v.y, v.w, 0x5410);
         o.w = __byte_perm(v.y, v.w, 0x7632);
-        reinterpret_cast<uint4*>(xstage)[wi] = o;
+        const int grp = wi >> 4, t = (wi >> 2) & 3, w = wi & 3;
+        *reinterpret_cast<uint4*>(xs + xperm_word(grp, t) + 4 * w) = o;
         part = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) +
                bf16_bits_to_f32(v.y & 0xFFFF) + bf16_bits_to_f32(v.y >> 16) +
                bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
@@ -373,123 +372,308 @@ gemv_ring_kernel(const GemvParams p, unsigned* err) {
       if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
     }
   }
-  named_bar(1, kRingConsumers * 32);
-  const int g0 = warp * GW;
-  uint32_t xf[GW][16];
-  float bias[GW];
-#pragma unroll
-  for (int gi = 0; gi < GW; ++gi) {
-    const int grp = min(g0 + gi, G - 1);
-    const uint4* bp = reinterpret_cast<const uint4*>(xstage + grp * 64 + tq * 16);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 b = bp[q];
-      xf[gi][4 * q + 0] = b.x; xf[gi][4 * q + 1] = b.y;
-      xf[gi][4 * q + 2] = b.z; xf[gi][4 * q + 3] = b.w;
-    }
-    bias[gi] = kNibbleBias * gsum[grp];
-  }
+  __syncthreads();
 
-  bool ok = true;
-  for (int i = 0; i < ntile; ++i) {
-    const int s = i % kRingStages;
-    if (ok) ok = mbar_wait(&full[s], (i / kRingStages) & 1, err);
-    const uint8_t* st = smem + s * geo.stage_bytes;
-    const uint8_t* rowa = st + gq * geo.row_stride;
-    const uint8_t* rowbp = st + (gq + 8) * geo.row_stride;
-    const uint16_t* sca = reinterpret_cast<const uint16_t*>(st + 16 * geo.row_stride + gq * geo.scb);
-    const uint16_t* scbp = reinterpret_cast<const uint16_t*>(st + 16 * geo.row_stride +
-                                                             (gq + 8) * geo.scb);
-    float acc_a = 0.f, acc_b = 0.f;
-    if (ok) {
+  float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll
+  for (int u = 0; u < kCpaMaxGroupsPerWarp; ++u) {
+    if (u < ng) {
+      const int grp = warp + kGemvWarps * u;
+      cp_async_wait(ng - 1 - u);
+      const uint4 wa = *reinterpret_cast<const uint4*>(wbuf + (u * 2 + 0) * 512 + lane * 16);
+      const uint4 wb = *reinterpret_cast<const uint4*>(wbuf + (u * 2 + 1) * 512 + lane * 16);
+      const uint4* bp = reinterpret_cast<const uint4*>(xs + xperm_word(grp, tq));
+      const uint4 b01 = bp[0], b23 = bp[1], b45 = bp[2], b67 = bp[3];
+      const uint32_t bw[16] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w,
+                               b45.x, b45.y, b45.z, b45.w, b67.x, b67.y, b67.z, b67.w};
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      group_mma(wa, wb, bw, d0, d1);
+      const float bias = kNibbleBias * gsum[grp];
+      acc_a = fmaf(sca[u], (d0[0] + d1[0]) - bias, acc_a);
+      acc_b = fmaf(scb[u], (d0[2] + d1[2]) - bias, acc_b);
+    }
+  }
+  pdl_launch_dependents();
+  if (tq == 0) {
+    red[warp * 16 + gq] = acc_a;
+    red[warp * 16 + gq + 8] = acc_b;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    const int j = tile0 + threadIdx.x;
+    if (j < n_out) {
+      float v = red[threadIdx.x];
+#pragma unroll
+      for (int w = 1; w < kGemvWarps; ++w) v += red[w * 16 + threadIdx.x];
+      const bool ok = (threadIdx.x < 8) ? oka : okb;
+      uint16_t o;
+      if (!ok) {
+        o = 0;
+      } else if (EPI == EPI_PLAIN) {
+        o = f32_to_bf16_bits(v);
+      } else if (EPI == EPI_SILU) {
+        o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+        hist_count(p.hist, o);
+      } else {
+        o = f32_to_bf16_bits(bf16_bits_to_f32(p.g[p.gid[j]]) * round_bf16(v));
+      }
+      p.out[j] = o;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent pipelined variant (default when in_features % 1024 == 0).
+// One CTA of 16 warps per SM walks a contiguous range of 16-row tiles as two
+// warp groups of 8 that take alternate tiles.  In a warp group, warp w owns
+// the K-slice of groups [w*GW, (w+1)*GW).  Every thread keeps the next tile
+// of its own weight bytes in flight with cp.async (a commit group per tile),
+// so HBM requests continue while the tensor cores work; with 16 warps per SM
+// four warps per scheduler hide the MMA and shared-memory latencies.  Per
+// tile: wait, group barrier (the tile's scale rows were copied by other
+// threads of the group), MMA, fixed-order combine of the 8 K-slices.  The
+// row pointers and the epilogue's per-row data (validity, g[channel]) are
+// resolved once in the prologue so no global load sits on the per-tile path.
+constexpr int kPipeGroupWarps = 8;
+constexpr int kPipeWarps = 2 * kPipeGroupWarps;
+constexpr int kPipeThreads = kPipeWarps * 32;
+constexpr int kPipeDepth = 2;  // tiles per warp group in flight (incl. current)
+
+struct PipeGeom {
+  int gw, wslot, scb, sc_slot, ring_off, sc_off, ptr_off, info_off, x_off, gsum_off, red_off,
+      total;
+};
+__host__ __device__ inline PipeGeom pipe_geom(int in, int max_tiles) {
+  PipeGeom g;
+  const int G = in / kGroup;
+  g.gw = G / kPipeGroupWarps;
+  g.wslot = g.gw * 1024;  // per warp per tile: GW groups x 2 rows x 512 B
+  g.scb = G * 2;
+  g.sc_slot = 16 * g.scb;
+  g.ring_off = 0;
+  g.sc_off = kPipeWarps * kPipeDepth * g.wslot;
+  g.ptr_off = g.sc_off + 2 * kPipeDepth * g.sc_slot;
+  g.info_off = g.ptr_off + max_tiles * 16 * 16;  // (qw, sc) pointers per row
+  g.x_off = g.info_off + max_tiles * 16 * 4;     // per-row epilogue value
+  g.gsum_off = g.x_off + G * 72 * 4;
+  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
+  g.total = g.red_off + 2 * 2 * kPipeGroupWarps * 16 * 4;
+  return g;
+}
+
+template <int MODE, int EPI, int GW>
+__global__ void __launch_bounds__(kPipeThreads, 1)
+gemv_pipe_kernel(const GemvParams p, int max_tiles) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int in = p.in_features;
+  const int G = in / kGroup;
+  const PipeGeom geo = pipe_geom(in, max_tiles);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wg = warp / kPipeGroupWarps, kw = warp % kPipeGroupWarps, gtid = tid % 256;
+  const int gq = lane >> 2, tq = lane & 3;
+  const uint8_t** rq = reinterpret_cast<const uint8_t**>(smem + geo.ptr_off);
+  const uint16_t** rs = reinterpret_cast<const uint16_t**>(smem + geo.ptr_off) + max_tiles * 16;
+  float* info = reinterpret_cast<float*>(smem + geo.info_off);  // NaN marks an invalid row
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + geo.x_off);
+  float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
+  float* red = reinterpret_cast<float*>(smem + geo.red_off) + wg * 2 * kPipeGroupWarps * 16;
+
+  if (MODE != ROW_DENSE) pdl_wait();
+  int n_out = p.n_out;
+  if (p.count) n_out = min(n_out, *p.count);
+  const int nt = (n_out + 15) / 16;
+  const int t0 = (int)((int64_t)nt * blockIdx.x / gridDim.x);
+  const int t1 = (int)((int64_t)nt * (blockIdx.x + 1) / gridDim.x);
+  const int ntile = t1 - t0;
+  for (int r = tid; r < ntile * 16; r += kPipeThreads) {
+    const int j = min(t0 * 16 + r, n_out - 1);
+    const uint8_t* qw;
+    const uint16_t* sc;
+    const bool ok = resolve_row<MODE>(p, j, qw, sc);
+    rq[r] = qw;
+    rs[r] = sc;
+    float v = ok ? 0.f : __int_as_float(0x7FC00000);
+    if (EPI == EPI_H && ok) v = bf16_bits_to_f32(p.g[p.gid[j]]);
+    info[r] = v;
+  }
+  __syncthreads();
+
+  // This warp group's tiles: local tiles wg, wg+2, ...; n_mine of them.
+  const int n_mine = (ntile - wg + 1) / 2;
+  const int nsc_chunks = 16 * geo.scb / 16;
+  const int sc_per_row = geo.scb / 16;
+  auto issue = [&](int m) {  // m-th tile of this warp group
+    if (m < n_mine) {
+      const int i = wg + 2 * m;
+      uint8_t* ws = smem + geo.ring_off + (warp * kPipeDepth + m % kPipeDepth) * geo.wslot;
+      const uint8_t* qa = rq[i * 16 + gq];
+      const uint8_t* qb = rq[i * 16 + gq + 8];
 #pragma unroll
       for (int gi = 0; gi < GW; ++gi) {
-        const int grp = g0 + gi;
-        if (grp < G) {
-          const uint4 wa = *reinterpret_cast<const uint4*>(rowa + grp * kGroupBytes + tq * 16);
-          const uint4 wb = *reinterpret_cast<const uint4*>(rowbp + grp * kGroupBytes + tq * 16);
-          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-          group_mma(wa, wb, xf[gi], d0, d1);
-          acc_a = fmaf(bf16_bits_to_f32(sca[grp]), (d0[0] + d1[0]) - bias[gi], acc_a);
-          acc_b = fmaf(bf16_bits_to_f32(scbp[grp]), (d0[2] + d1[2]) - bias[gi], acc_b);
-        }
+        const int off = (kw * GW + gi) * kGroupBytes + tq * 16;
+        cp_async16(ws + (gi * 2 + 0) * 512 + lane * 16, qa + off);
+        cp_async16(ws + (gi * 2 + 1) * 512 + lane * 16, qb + off);
+      }
+      uint8_t* sdst = smem + geo.sc_off + (wg * kPipeDepth + m % kPipeDepth) * geo.sc_slot;
+      for (int c = gtid; c < nsc_chunks; c += 256) {
+        const int row = c / sc_per_row, part = c % sc_per_row;
+        cp_async16(sdst + row * geo.scb + part * 16, rs[i * 16 + row] + part * 8);
       }
     }
-    float* rr = red + (i & 1) * kRingConsumers * 16;
-    if (tq == 0) {
-      rr[warp * 16 + gq] = acc_a;
-      rr[warp * 16 + gq + 8] = acc_b;
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int m = 0; m < kPipeDepth - 1; ++m) issue(m);
+
+  if (MODE == ROW_DENSE) pdl_wait();
+  {
+    const int nwords = in / 8;
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+    for (int wi = tid; wi < ((nwords + kPipeThreads - 1) / kPipeThreads) * kPipeThreads;
+         wi += kPipeThreads) {
+      float part = 0.f;
+      if (wi < nwords) {
+        const uint4 v = __ldg(xv + wi);
+        uint4 o;
+        o.x = __byte_perm(v.x, v.z, 0x5410);
+        o.y = __byte_perm(v.x, v.z, 0x7632);
+        o.z = __byte_perm(v.y, v.w, 0x5410);
+        o.w = __byte_perm(v.y, v.w, 0x7632);
+        const int grp = wi >> 4, t = (wi >> 2) & 3, w = wi & 3;
+        *reinterpret_cast<uint4*>(xs + xperm_word(grp, t) + 4 * w) = o;
+        part = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) +
+               bf16_bits_to_f32(v.y & 0xFFFF) + bf16_bits_to_f32(v.y >> 16) +
+               bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
+               bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 8);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
     }
-    named_bar(1, kRingConsumers * 32);
-    if (ctid == 0) mbar_arrive(&empty[s]);
-    if (warp == 0 && lane < 16) {
+  }
+  __syncthreads();
+  float bias[GW];
+#pragma unroll
+  for (int gi = 0; gi < GW; ++gi) bias[gi] = kNibbleBias * gsum[kw * GW + gi];
+
+  for (int m = 0; m < n_mine; ++m) {
+    issue(m + kPipeDepth - 1);
+    cp_async_wait(kPipeDepth - 1);
+    named_bar(1 + wg, 256);  // scale rows of this tile (other threads' copies) visible
+    const int i = wg + 2 * m;
+    const uint8_t* ws = smem + geo.ring_off + (warp * kPipeDepth + m % kPipeDepth) * geo.wslot;
+    const uint8_t* sbase = smem + geo.sc_off + (wg * kPipeDepth + m % kPipeDepth) * geo.sc_slot;
+    const uint16_t* sca = reinterpret_cast<const uint16_t*>(sbase + gq * geo.scb);
+    const uint16_t* scbp = reinterpret_cast<const uint16_t*>(sbase + (gq + 8) * geo.scb);
+    float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < GW; ++gi) {
+      const int grp = kw * GW + gi;
+      const uint4 wa = *reinterpret_cast<const uint4*>(ws + (gi * 2 + 0) * 512 + lane * 16);
+      const uint4 wb = *reinterpret_cast<const uint4*>(ws + (gi * 2 + 1) * 512 + lane * 16);
+      const uint4* bp = reinterpret_cast<const uint4*>(xs + xperm_word(grp, tq));
+      const uint4 b01 = bp[0], b23 = bp[1], b45 = bp[2], b67 = bp[3];
+      const uint32_t bw[16] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w,
+                               b45.x, b45.y, b45.z, b45.w, b67.x, b67.y, b67.z, b67.w};
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      group_mma(wa, wb, bw, d0, d1);
+      acc_a = fmaf(bf16_bits_to_f32(sca[grp]), (d0[0] + d1[0]) - bias[gi], acc_a);
+      acc_b = fmaf(bf16_bits_to_f32(scbp[grp]), (d0[2] + d1[2]) - bias[gi], acc_b);
+    }
+    float* rr = red + (m & 1) * kPipeGroupWarps * 16;
+    if (tq == 0) {
+      rr[kw * 16 + gq] = acc_a;
+      rr[kw * 16 + gq + 8] = acc_b;
+    }
+    named_bar(1 + wg, 256);
+    if (kw == 0 && lane < 16) {
       const int j = (t0 + i) * 16 + lane;
-      if (j < n_out && ok) {
+      if (j < n_out) {
         float v = rr[lane];
 #pragma unroll
-        for (int w = 1; w < kRingConsumers; ++w) v += rr[w * 16 + lane];
-        const uint8_t* dq;
-        const uint16_t* ds;
-        const bool valid = resolve_row<MODE>(p, j, dq, ds);
+        for (int w = 1; w < kPipeGroupWarps; ++w) v += rr[w * 16 + lane];
+        const float inf = info[i * 16 + lane];
         uint16_t o;
-        if (!valid) o = 0;
-        else if (EPI == EPI_PLAIN) o = f32_to_bf16_bits(v);
-        else if (EPI == EPI_SILU) {
+        if (inf != inf) {
+          o = 0;  // invalid row index
+        } else if (EPI == EPI_PLAIN) {
+          o = f32_to_bf16_bits(v);
+        } else if (EPI == EPI_SILU) {
           o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
           hist_count(p.hist, o);
+        } else {
+          o = f32_to_bf16_bits(inf * round_bf16(v));
         }
-        else o = f32_to_bf16_bits(bf16_bits_to_f32(p.g[p.gid[j]]) * round_bf16(v));
         p.out[j] = o;
       }
     }
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   pdl_launch_dependents();
 }
 
 template <int MODE, int EPI, int GW>
-static int launch_ring(const GemvParams& p, cudaStream_t s) {
-  const RingGeom geo = ring_geom(p.in_features);
-  auto kern = gemv_ring_kernel<MODE, EPI, GW>;
+static int launch_pipe(const GemvParams& p, cudaStream_t s) {
+  const int nt = (p.n_out + 15) / 16;
+  const int grid = nt < num_sms() ? nt : num_sms();
+  const int max_tiles = (nt + grid - 1) / grid;
+  const PipeGeom geo = pipe_geom(p.in_features, max_tiles);
+  auto kern = gemv_pipe_kernel<MODE, EPI, GW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        geo.total);
   if (e != cudaSuccess) return launch_status(e);
-  const int nt = (p.n_out + 15) / 16;
-  const int grid = nt < num_sms() ? nt : num_sms();
-  unsigned* err = error_word_ptr();
-  if (!err) return DIP_ERR_CUDA;
-  return launch_status(launch(kern, dim3(grid), dim3(kRingThreads), (size_t)geo.total, s, p, err));
+  return launch_status(launch(kern, dim3(grid), dim3(kPipeThreads), (size_t)geo.total, s, p,
+                              max_tiles));
 }
 
-// The ring kernel needs whole 8-group K-slices (G % 8 == 0) so every row's
-// scales are a 16-byte multiple, and its ring must fit in shared memory.
-static bool ring_ok(const GemvParams& p) {
+static bool pipe_ok(const GemvParams& p) {
   const int G = p.in_features / kGroup;
-  if (G % 8 != 0 || G / 8 > 8) return false;
-  if (ring_geom(p.in_features).total > 220 * 1024) return false;
+  if (G % kPipeGroupWarps != 0 || G / kPipeGroupWarps > 6) return false;
   if ((reinterpret_cast<uintptr_t>(p.sc0) & 15) != 0) return false;
   if (p.qw1 && (reinterpret_cast<uintptr_t>(p.sc1) & 15) != 0) return false;
-  return true;
+  const int nt = (p.n_out + 15) / 16;
+  const int grid = nt < num_sms() ? nt : num_sms();
+  return pipe_geom(p.in_features, (nt + grid - 1) / grid).total <= 225 * 1024;
 }
 
 template <int MODE, int EPI>
-static int launch_ring_any(const GemvParams& p, cudaStream_t s) {
-  switch (p.in_features / kGroup / 8) {
-    case 1: return launch_ring<MODE, EPI, 1>(p, s);
-    case 2: return launch_ring<MODE, EPI, 2>(p, s);
-    case 3: return launch_ring<MODE, EPI, 3>(p, s);
-    case 4: return launch_ring<MODE, EPI, 4>(p, s);
-    case 5: return launch_ring<MODE, EPI, 5>(p, s);
-    case 6: return launch_ring<MODE, EPI, 6>(p, s);
-    case 7: return launch_ring<MODE, EPI, 7>(p, s);
-    default: return launch_ring<MODE, EPI, 8>(p, s);
+static int launch_pipe_any(const GemvParams& p, cudaStream_t s) {
+  switch (p.in_features / kGroup / kPipeGroupWarps) {
+    case 1: return launch_pipe<MODE, EPI, 1>(p, s);
+    case 2: return launch_pipe<MODE, EPI, 2>(p, s);
+    case 3: return launch_pipe<MODE, EPI, 3>(p, s);
+    case 4: return launch_pipe<MODE, EPI, 4>(p, s);
+    case 5: return launch_pipe<MODE, EPI, 5>(p, s);
+    default: return launch_pipe<MODE, EPI, 6>(p, s);
   }
+}
+
+static bool cpa_ok(const GemvParams& p) {
+  const int G = p.in_features / kGroup;
+  return (G + kGemvWarps - 1) / kGemvWarps <= kCpaMaxGroupsPerWarp;
+}
+
+template <int MODE, int EPI>
+static int launch_cpa(const GemvParams& p, cudaStream_t s) {
+  const CpaGeom geo = cpa_geom(p.in_features);
+  auto kern = gemv_cpa_kernel<MODE, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       geo.total);
+  if (e != cudaSuccess) return launch_status(e);
+  const dim3 grid((p.n_out + 15) / 16);
+  return launch_status(launch(kern, grid, dim3(kGemvThreads), (size_t)geo.total, s, p));
 }
 
 // Host launcher shared by the entry points below.
 template <int MODE, int EPI>
 static int launch_gemv(const GemvParams& p, cudaStream_t s) {
   if (p.n_out == 0) return DIP_OK;
-  if (ring_ok(p) && !force_simple_gemv()) return launch_ring_any<MODE, EPI>(p, s);
+  if (!force_simple_gemv()) {
+    if (pipe_ok(p)) return launch_pipe_any<MODE, EPI>(p, s);
+    if (cpa_ok(p)) return launch_cpa<MODE, EPI>(p, s);
+  }
   const int G = p.in_features / kGroup;
   const size_t smem = (size_t)p.in_features * 2 + (size_t)G * 4 + kGemvWarps * 16 * 4;
   auto kern = gemv_int4_kernel<MODE, EPI>;

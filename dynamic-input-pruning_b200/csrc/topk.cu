@@ -21,6 +21,16 @@
 namespace dip {
 
 constexpr int kTopkThreads = 1024;
+
+// Phase tracing (compile with -DDIP_TRACE): thread 0 of block 0 records the
+// SM clock at numbered points into dip_trace_clock[].
+#ifdef DIP_TRACE
+__device__ long long dip_trace_clock[16];
+#define DIP_TRACE_POINT(n) \
+  do { if (threadIdx.x == 0 && blockIdx.x == 0) dip_trace_clock[n] = clock64(); } while (0)
+#else
+#define DIP_TRACE_POINT(n) do { } while (0)
+#endif
 constexpr int kTopkMaxN = 98304;  // keys kept in shared memory (2 B each)
 constexpr uint16_t kNanKey = 0xFFFF;  // as a float pattern (<<16) this is a NaN
 
@@ -53,6 +63,44 @@ __device__ __forceinline__ int2 block_excl_scan2(int a, int b, int2* warp_tot, i
   const int2 wbase = warp_tot[warp];
   tot = warp_tot[32];
   return make_int2(wbase.x + ia - a, wbase.y + ib - b);
+}
+
+
+// Stable two-tier compaction of the index range [0, n): elements with
+// isA(i) go, in index order, to positions [0, nA); elements with isB(i) to
+// [nA, nA + nB) (the tiers are disjoint).  Each warp owns one contiguous
+// chunk and walks it 32 elements per round, so the positions written by one
+// store instruction are consecutive (coalesced), unlike a per-thread run.
+// emit(pos, i) is called once per selected element; tot = (nA, nB).
+template <class FA, class FB, class EMIT>
+__device__ __forceinline__ void block_compact2(int n, FA isA, FB isB, EMIT emit, int2* warp_tot,
+                                               int2& tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int chunk = (((n + nw - 1) / nw) + 31) & ~31;
+  const int beg = min(n, warp * chunk), end = min(n, beg + chunk);
+  int ca = 0, cb = 0;
+  for (int base = beg; base < end; base += 32) {
+    const int i = base + lane;
+    const bool a = i < end && isA(i);
+    const bool b = i < end && !a && isB(i);
+    ca += __popc(__ballot_sync(0xffffffffu, a));
+    cb += __popc(__ballot_sync(0xffffffffu, b));
+  }
+  const int2 off = block_excl_scan2(lane == 0 ? ca : 0, lane == 0 ? cb : 0, warp_tot, tot);
+  int pa = __shfl_sync(0xffffffffu, off.x, 0);
+  int pb = tot.x + __shfl_sync(0xffffffffu, off.y, 0);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = beg; base < end; base += 32) {
+    const int i = base + lane;
+    const bool a = i < end && isA(i);
+    const bool b = i < end && !a && isB(i);
+    const unsigned ma = __ballot_sync(0xffffffffu, a);
+    const unsigned mb = __ballot_sync(0xffffffffu, b);
+    if (a) emit(pa + __popc(ma & lt), i);
+    if (b) emit(pb + __popc(mb & lt), i);
+    pa += __popc(ma);
+    pb += __popc(mb);
+  }
 }
 
 // Find, scanning bins from the top, the bin holding the element of 1-based
@@ -231,23 +279,12 @@ topk_select_kernel(const uint16_t* __restrict__ s_all, int n, int k, int32_t* __
   __syncthreads();
   const float lo = s_lohi[0], hi = s_lohi[1];
 
-  // Compaction: thread tid owns the contiguous range [beg, end).
-  const int per = (n + kTopkThreads - 1) / kTopkThreads;
-  const int beg = min(n, tid * per), end = min(n, beg + per);
-  int ca = 0, cb = 0;
-  for (int i = beg; i < end; ++i) {
-    const float v = bf16_bits_to_f32(keys[i]);
-    ca += (v > hi);
-    cb += (v > lo && v <= hi);
-  }
+  // Compaction of the two tiers (ascending index within each).
   int2 tot;
-  const int2 off = block_excl_scan2(ca, cb, warp_tot, tot);
-  int pa = off.x, pb = tot.x + off.y;
-  for (int i = beg; i < end; ++i) {
-    const float v = bf16_bits_to_f32(keys[i]);
-    if (v > hi) { if (pa < k) idx[pa] = i; ++pa; }
-    else if (v > lo && v <= hi) { if (pb < k) idx[pb] = i; ++pb; }
-  }
+  block_compact2(
+      n, [&](int i) { return bf16_bits_to_f32(keys[i]) > hi; },
+      [&](int i) { const float v = bf16_bits_to_f32(keys[i]); return v > lo && v <= hi; },
+      [&](int pos, int i) { if (pos < k) idx[pos] = i; }, warp_tot, tot);
   pdl_launch_dependents();
   const int filled = min(k, tot.x + tot.y);
   for (int i = filled + tid; i < k; i += kTopkThreads) idx[i] = 0;
@@ -261,20 +298,12 @@ shard_select_kernel(const int32_t* __restrict__ idx, int k, int lo, int hi,
                     int32_t* __restrict__ local, int32_t* __restrict__ count) {
   __shared__ int2 warp_tot[33];
   pdl_wait();
-  const int tid = threadIdx.x;
-  const int per = (k + kTopkThreads - 1) / kTopkThreads;
-  const int beg = min(k, tid * per), end = min(k, beg + per);
-  int c = 0;
-  for (int j = beg; j < end; ++j) c += (idx[j] >= lo && idx[j] < hi);
   int2 tot;
-  const int2 off = block_excl_scan2(c, 0, warp_tot, tot);
-  int pos = off.x;
-  for (int j = beg; j < end; ++j) {
-    const int v = idx[j];
-    if (v >= lo && v < hi) local[pos++] = v - lo;
-  }
+  block_compact2(
+      k, [&](int j) { return idx[j] >= lo && idx[j] < hi; }, [&](int) { return false; },
+      [&](int pos, int j) { local[pos] = idx[j] - lo; }, warp_tot, tot);
   pdl_launch_dependents();
-  if (tid == 0) count[0] = tot.x;
+  if (threadIdx.x == 0) count[0] = tot.x;
 }
 
 // Cache hit/miss split (dip_ca.py:137-142 with the src/row tables of
@@ -285,26 +314,23 @@ ca_split_kernel(const int32_t* __restrict__ idx, int k, const int64_t* __restric
                 int32_t* __restrict__ row, int32_t* __restrict__ n_hit) {
   __shared__ int2 warp_tot[33];
   pdl_wait();
-  const int tid = threadIdx.x;
-  const int per = (k + kTopkThreads - 1) / kTopkThreads;
-  const int beg = min(k, tid * per), end = min(k, beg + per);
-  int ch = 0, cm = 0;
-  for (int j = beg; j < end; ++j) {
+  auto slot_of = [&](int j) -> int64_t {
     const int c = idx[j];
-    const int64_t sl = (c >= 0 && c < n_channels) ? id2slot[c] : -1;
-    if (sl >= 0) ++ch; else ++cm;
-  }
+    return (c >= 0 && c < n_channels) ? id2slot[c] : -1;
+  };
   int2 tot;
-  const int2 off = block_excl_scan2(ch, cm, warp_tot, tot);
-  int ph = off.x, pm = tot.x + off.y;
-  for (int j = beg; j < end; ++j) {
-    const int c = idx[j];
-    const int64_t sl = (c >= 0 && c < n_channels) ? id2slot[c] : -1;
-    if (sl >= 0) { combined[ph] = c; src[ph] = 0; row[ph] = (int32_t)sl; ++ph; }
-    else { combined[pm] = c; src[pm] = 1; row[pm] = c; ++pm; }
-  }
+  block_compact2(
+      k, [&](int j) { return slot_of(j) >= 0; }, [&](int j) { return slot_of(j) < 0; },
+      [&](int pos, int j) {
+        const int c = idx[j];
+        const int64_t sl = slot_of(j);
+        combined[pos] = c;
+        src[pos] = sl >= 0 ? 0 : 1;
+        row[pos] = sl >= 0 ? (int32_t)sl : c;
+      },
+      warp_tot, tot);
   pdl_launch_dependents();
-  if (tid == 0) n_hit[0] = tot.x;
+  if (threadIdx.x == 0) n_hit[0] = tot.x;
 }
 
 // ---------------------------------------------------------------------------
@@ -337,6 +363,7 @@ topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __r
   const int tid = threadIdx.x;
   if (tid == 0) { s_max = 0; s_w = 0; }
   pdl_wait();
+  DIP_TRACE_POINT(0);
   // Thread tid owns bins [32 tid, 32 tid + 32): counts, then zero them.
   uint4* hv = reinterpret_cast<uint4*>(hist) + tid * 8;
   unsigned c[32];
@@ -358,22 +385,29 @@ topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __r
     reinterpret_cast<uint4*>(keys)[v] = r;
   }
   for (int i = nvec * 8 + tid; i < n; i += kTopkThreads) keys[i] = s[i] & 0x7FFF;
+  DIP_TRACE_POINT(1);
   int2 tot;
   const int2 pre = block_excl_scan2(tot_mine, 0, warp_tot, tot);  // also a barrier
+  DIP_TRACE_POINT(2);
   const int nvalid = tot.x;
   const int above = nvalid - pre.x - tot_mine;  // count in bins above my range
-  if (tot_mine > 0) {
-    int top = 31;
-    while (c[top] == 0) --top;
-    atomicMax(&s_max, (unsigned)(tid * 32 + top));
-  }
+  // Fully unrolled scans keep c[] in registers.
+  int top = -1;
+#pragma unroll
+  for (int b = 0; b < 32; ++b) if (c[b] != 0) top = b;
+  unsigned mkey = top >= 0 ? (unsigned)(tid * 32 + top) : 0u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mkey = max(mkey, __shfl_xor_sync(0xffffffffu, mkey, o));
+  if ((tid & 31) == 0 && mkey) atomicMax(&s_max, mkey);
   const bool has_w = nvalid >= k + 1;
   if (has_w && above < k + 1 && k + 1 <= above + tot_mine) {
-    int run = above;
+    int run = above, found = -1;
+#pragma unroll
     for (int b = 31; b >= 0; --b) {
       run += c[b];
-      if (run >= k + 1) { s_w = (unsigned)(tid * 32 + b); break; }
+      if (found < 0 && run >= k + 1) found = b;
     }
+    s_w = (unsigned)(tid * 32 + found);
   }
   __syncthreads();
   if (tid == 0) {
@@ -390,25 +424,231 @@ topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __r
   }
   __syncthreads();
   const float lo = s_lohi[0], hi = s_lohi[1];
-  const int per = (n + kTopkThreads - 1) / kTopkThreads;
-  const int beg = min(n, tid * per), end = min(n, beg + per);
-  int ca = 0, cb = 0;
-  for (int i = beg; i < end; ++i) {
-    const float v = bf16_bits_to_f32(keys[i]);
-    ca += (v > hi);
-    cb += (v > lo && v <= hi);
-  }
-  const int2 off = block_excl_scan2(ca, cb, warp_tot, tot);
-  int pa = off.x, pb = tot.x + off.y;
-  for (int i = beg; i < end; ++i) {
-    const float v = bf16_bits_to_f32(keys[i]);
-    if (v > hi) { if (pa < k) idx[pa] = i; ++pa; }
-    else if (v > lo && v <= hi) { if (pb < k) idx[pb] = i; ++pb; }
-  }
+  DIP_TRACE_POINT(3);
+  block_compact2(
+      n, [&](int i) { return bf16_bits_to_f32(keys[i]) > hi; },
+      [&](int i) { const float v = bf16_bits_to_f32(keys[i]); return v > lo && v <= hi; },
+      [&](int pos, int i) { if (pos < k) idx[pos] = i; }, warp_tot, tot);
+  DIP_TRACE_POINT(4);
   pdl_launch_dependents();
   const int filled = min(k, tot.x + tot.y);
   for (int i = filled + tid; i < k; i += kTopkThreads) idx[i] = 0;
+  DIP_TRACE_POINT(5);
 }
+
+// ---------------------------------------------------------------------------
+// Top-k v3: select from a two-level histogram, compact on many SMs.
+//
+// Scratch (dip_topk_hist_bytes): fine[32768] counts of the 15-bit |s| key,
+// coarse[256] counts of its exponent byte, status[64] look-back words.  It
+// must be zero on entry.  The selection reads only the coarse histogram and
+// three 128-bin slices of the fine one, so no SM moves more than a few
+// hundred bytes of it.  Each CTA then compacts its own 2048-element chunk:
+// the two tier counts of earlier chunks come from a bounded decoupled
+// look-back on status[], and the total of tier A (needed to place tier B)
+// comes from the histogram, so no CTA waits on a later one.
+constexpr int kCoarseOff = kHistBins;                 // in u32 words
+constexpr int kStatusOffBytes = (kHistBins + 256) * 4;
+constexpr int kCompactChunk = 2048;                   // elements per CTA
+constexpr int kMaxCompactCtas = 64;
+constexpr size_t kTopkScratchBytes = kStatusOffBytes + kMaxCompactCtas * 8;
+
+// #{keys > t} from the histograms (t >= 0, fp32): keys above bf16 bin b0 =
+// (bits(t) >> 16) are all keys with key >= b0 + 1.  One warp.
+__device__ __forceinline__ int warp_count_above(const unsigned* hist, const int* coarse_suffix,
+                                                float t) {
+  const int lane = threadIdx.x & 31;
+  const int kmin = (int)(__float_as_uint(t) >> 16) + 1;  // smallest key counted
+  if (kmin > 0x7F80) return 0;
+  const int cb = kmin >> 7;
+  int part = 0;
+  for (int f = lane; f < 128; f += 32) {
+    const int key = (cb << 7) | f;
+    if (key >= kmin) part += hist[key];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  return part + (cb < 255 ? coarse_suffix[cb + 1] : 0);
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+topk_compact_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __restrict__ idx,
+                    unsigned* __restrict__ scratch, unsigned* err) {
+  __shared__ int coarse_suffix[257];   // coarse_suffix[b] = #keys with exponent byte >= b
+  __shared__ uint16_t keys[kCompactChunk];
+  __shared__ int2 warp_tot[33];
+  __shared__ float s_lohi[2];
+  __shared__ int s_tot[2];              // #(> hi), #(> lo)
+  __shared__ int2 s_off;                // tier A / B counts of earlier chunks
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c0 = blockIdx.x * kCompactChunk;
+  const int cn = min(kCompactChunk, n - c0);
+  unsigned long long* status =
+      reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(scratch) + kStatusOffBytes);
+  pdl_wait();
+  // Keys of this chunk (two per thread).
+  for (int e = tid; e < cn; e += kTopkThreads) keys[e] = s[c0 + e] & 0x7FFF;
+  if (warp == 0) {
+    // Coarse histogram: suffix sums, total, the bins of w and of max.
+    const unsigned* coarse = scratch + kCoarseOff;
+    int cnt[8], loc = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { cnt[q] = coarse[255 - (lane * 8 + q)]; loc += cnt[q]; }
+    int incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int run = incl - loc;  // count in bins above this lane's
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { run += cnt[q]; coarse_suffix[255 - (lane * 8 + q)] = run; }
+    if (lane == 0) coarse_suffix[256] = 0;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nvalid = coarse_suffix[0];
+    const bool has_w = nvalid >= k + 1;
+    // highest non-empty coarse bin, then the highest non-empty key in it
+    int topb = -1;
+    for (int b = lane; b < 256; b += 32)
+      if (coarse_suffix[b] - coarse_suffix[b + 1] > 0) topb = max(topb, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) topb = max(topb, __shfl_xor_sync(0xffffffffu, topb, o));
+    int maxkey = 0;
+    if (topb >= 0) {
+      int mk = -1;
+      for (int f = lane; f < 128; f += 32)
+        if (scratch[(topb << 7) | f] != 0) mk = max(mk, (topb << 7) | f);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mk = max(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+      maxkey = max(mk, 0);
+    }
+    float wv = 0.f;
+    if (has_w) {
+      // coarse bin b1 holding rank k+1 from the top: suffix[b1+1] < k+1 <= suffix[b1]
+      int b1 = -1;
+      for (int b = lane; b < 256; b += 32)
+        if (coarse_suffix[b + 1] < k + 1 && k + 1 <= coarse_suffix[b]) b1 = b;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) b1 = max(b1, __shfl_xor_sync(0xffffffffu, b1, o));
+      const int rank = k + 1 - coarse_suffix[b1 + 1];
+      // fine bins of b1 from the top: lane owns 4 consecutive bins
+      int f4[4], loc = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { f4[q] = scratch[(b1 << 7) | (127 - (lane * 4 + q))]; loc += f4[q]; }
+      int incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      int runf = incl - loc, found = -1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        runf += f4[q];
+        if (found < 0 && runf >= rank && runf - f4[q] < rank) found = 127 - (lane * 4 + q);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(0xffffffffu, found, o));
+      wv = bf16_bits_to_f32((unsigned)((b1 << 7) | found));
+    }
+    // The reference's host loop, step for step, in fp32 round-to-nearest.
+    float hi = bf16_bits_to_f32((unsigned)maxkey), lo = 0.0f;
+    float t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    for (int step = 0; step < 25; ++step) {
+      if (has_w && wv > t) lo = t; else hi = t;
+      t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    }
+    const int n_hi = warp_count_above(scratch, coarse_suffix, hi);
+    const int n_lo = warp_count_above(scratch, coarse_suffix, lo);
+    if (lane == 0) { s_lohi[0] = lo; s_lohi[1] = hi; s_tot[0] = n_hi; s_tot[1] = n_lo; }
+  }
+  __syncthreads();
+  const float lo = s_lohi[0], hi = s_lohi[1];
+  auto isA = [&](int e) { return bf16_bits_to_f32(keys[e]) > hi; };
+  auto isB = [&](int e) { const float v = bf16_bits_to_f32(keys[e]); return v > lo && v <= hi; };
+  // Chunk counts -> publish -> look back over earlier chunks.
+  int ca = 0, cb = 0;
+  for (int e = tid; e < cn; e += kTopkThreads) { ca += isA(e); cb += isB(e); }
+  int2 tot;
+  block_excl_scan2(ca, cb, warp_tot, tot);
+  if (tid == 0) {
+    const unsigned long long word = (1ull << 63) | ((unsigned long long)tot.x << 32) | (unsigned)tot.y;
+    asm volatile("st.release.gpu.global.u64 [%0], %1;\n" ::"l"(status + blockIdx.x), "l"(word)
+                 : "memory");
+  }
+  if (warp == 0) {
+    int pa = 0, pb = 0;
+    for (int c = lane; c < (int)blockIdx.x; c += 32) {
+      unsigned long long v = 0;
+      for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(status + c) : "memory");
+        if (v >> 63) break;
+      }
+      if (!(v >> 63)) { atomicOr(err, kErrTimeout); v = 0; }
+      pa += (int)((v >> 32) & 0x7FFFFFFF);
+      pb += (int)(v & 0xFFFFFFFFu);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      pa += __shfl_xor_sync(0xffffffffu, pa, o);
+      pb += __shfl_xor_sync(0xffffffffu, pb, o);
+    }
+    if (lane == 0) s_off = make_int2(pa, pb);
+  }
+  __syncthreads();
+  const int baseA = s_off.x, baseB = s_tot[0] + s_off.y;
+  int2 tot2;
+  block_compact2(
+      cn, isA, isB,
+      [&](int pos, int e) {
+        const int p = pos < tot.x ? baseA + pos : baseB + (pos - tot.x);
+        if (p < k) idx[p] = c0 + e;
+      },
+      warp_tot, tot2);
+  pdl_launch_dependents();
+  // Unfilled tail (only when fewer than k keys qualify): zeros, as the reference.
+  const int filled = min(k, s_tot[1]);
+  const int per = (k - filled + gridDim.x - 1) / gridDim.x;
+  const int z0 = filled + blockIdx.x * per, z1 = min(k, z0 + per);
+  for (int i = z0 + tid; i < z1; i += kTopkThreads) idx[i] = 0;
+}
+
+// Clears the top-k scratch (histograms and look-back words); grid-stride.
+__global__ void zero_words_kernel(uint4* __restrict__ p, int n16) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x)
+    p[i] = make_uint4(0, 0, 0, 0);
+  pdl_launch_dependents();
+}
+
+__global__ void __launch_bounds__(256)
+topk_hist2_kernel(const uint16_t* __restrict__ s, int n, unsigned* __restrict__ scratch) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned key = s[i] & 0x7FFFu;
+    if (key <= 0x7F80u) {
+      atomicAdd(&scratch[key], 1u);
+      atomicAdd(&scratch[kCoarseOff + (key >> 7)], 1u);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+int topk_compact_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, unsigned* scratch,
+                        cudaStream_t st) {
+  if (n < 1 || n > kMaxCompactCtas * kCompactChunk || k < 1 || k > INT32_MAX || !s || !idx ||
+      !scratch)
+    return DIP_ERR_ARG;
+  unsigned* err = error_word_ptr();
+  if (!err) return DIP_ERR_CUDA;
+  const int grid = (int)((n + kCompactChunk - 1) / kCompactChunk);
+  return launch_status(launch(topk_compact_kernel, dim3(grid), dim3(kTopkThreads), 0, st, s,
+                              (int)n, (int)k, idx, scratch, err));
+}
+
+size_t topk_scratch_bytes() { return kTopkScratchBytes; }
 
 int topk_from_hist_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx,
                           unsigned* hist, cudaStream_t st) {
@@ -473,16 +713,21 @@ extern "C" int dip_shard_select(const int32_t* idx, int64_t k, int64_t lo, int64
                               count));
 }
 
-extern "C" size_t dip_topk_hist_bytes(void) { return kHistBins * sizeof(unsigned); }
+extern "C" size_t dip_topk_hist_bytes(void) { return kTopkScratchBytes; }
 
 extern "C" int dip_topk_select_ws(const dip_bf16* s, int64_t n, int64_t k, int32_t* idx,
                                   void* hist, dip_stream_t stream) {
-  if (n < 1 || n > kTopkMaxN || k < 0 || k > INT32_MAX || !s || !hist) return DIP_ERR_ARG;
+  if (n < 1 || n > kMaxCompactCtas * kCompactChunk || k < 0 || k > INT32_MAX || !s || !hist)
+    return DIP_ERR_ARG;
   if (k == 0) return DIP_OK;
-  if (!idx) return DIP_ERR_ARG;
+  if (!idx || (reinterpret_cast<uintptr_t>(hist) & 15)) return DIP_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned* sc = static_cast<unsigned*>(hist);
   const int grid = (int)((n + 255) / 256 < 148 ? (n + 255) / 256 : 148);
-  int st = launch_status(launch(topk_hist_kernel, dim3(grid), dim3(256), 0, (cudaStream_t)stream,
-                                s, (int)n, static_cast<unsigned*>(hist)));
-  if (st) return st;
-  return topk_from_hist_launch(s, n, k, idx, static_cast<unsigned*>(hist), (cudaStream_t)stream);
+  int r = launch_status(launch(topk_hist2_kernel, dim3(grid), dim3(256), 0, st, s, (int)n, sc));
+  if (r) return r;
+  r = topk_compact_launch(s, n, k, idx, sc, st);
+  if (r) return r;
+  return launch_status(launch(zero_words_kernel, dim3(33), dim3(256), 0, st,
+                              reinterpret_cast<uint4*>(hist), (int)(kTopkScratchBytes / 16)));
 }

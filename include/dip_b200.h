@@ -191,12 +191,12 @@ typedef struct dip_layer {
 } dip_layer_t;
 
 DIP_API size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k);
-/* The workspace must be ZERO before its first use (its first 128 KB hold the
- * top-k histogram, which the gate kernel fills and the top-k clears); every
+/* The workspace must be ZERO before its first use (its first 130 KB hold the
+ * top-k histograms, which the gate kernel fills and the last kernel clears); every
  * call leaves that region zero, so a workspace can be reused call after call
  * on one stream. */
-/* The workspace must be ZERO before its first use (its first 128 KB hold the
- * top-k histogram, which the gate kernel fills and the top-k clears); every
+/* The workspace must be ZERO before its first use (its first 130 KB hold the
+ * top-k histograms, which the gate kernel fills and the last kernel clears); every
  * call leaves that region zero, so a workspace can be reused call after call
  * on one stream. */
 /* g_out (bf16[inter]) and idx_out (int32[k]) may be NULL; when given they
