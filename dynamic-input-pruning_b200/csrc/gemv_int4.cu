@@ -289,194 +289,61 @@ __device__ __forceinline__ void cp_async_wait(int n) {
 // at word 16 t + 4 (t >> 1), which puts the four quads in distinct banks.
 __device__ __forceinline__ int xperm_word(int grp, int t) { return grp * 72 + t * 16 + (t >> 1) * 4; }
 
-struct CpaGeom {
-  int ngw, warp_bytes, x_off, gsum_off, red_off, total;
-};
-__host__ __device__ inline CpaGeom cpa_geom(int in) {
-  CpaGeom g;
-  const int G = in / kGroup;
-  g.ngw = (G + kGemvWarps - 1) / kGemvWarps;
-  g.warp_bytes = g.ngw * 2 * 32 * 16;
-  g.x_off = kGemvWarps * g.warp_bytes;
-  g.gsum_off = g.x_off + G * 72 * 4;
-  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
-  g.total = g.red_off + kGemvWarps * 16 * 4;
-  return g;
-}
-
-template <int MODE, int EPI>
-__global__ void __launch_bounds__(kGemvThreads)
-gemv_cpa_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int in = p.in_features;
-  const int G = in / kGroup;
-  const CpaGeom geo = cpa_geom(in);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gq = lane >> 2, tq = lane & 3;
-  const int tile0 = blockIdx.x * 16;
-  uint8_t* wbuf = smem + warp * geo.warp_bytes;  // [u][row a/b][lane] x 16 B
-  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + geo.x_off);
-  float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
-  float* red = reinterpret_cast<float*>(smem + geo.red_off);
-
-  if (MODE != ROW_DENSE) pdl_wait();
-  int n_out = p.n_out;
-  if (p.count) n_out = min(n_out, *p.count);
-  if (tile0 >= n_out) return;
-  const int ja = min(tile0 + gq, n_out - 1);
-  const int jb = min(tile0 + gq + 8, n_out - 1);
-  const uint8_t *qa, *qb;
-  const uint16_t *sa_p, *sb_p;
-  const bool oka = resolve_row<MODE>(p, ja, qa, sa_p);
-  const bool okb = resolve_row<MODE>(p, jb, qb, sb_p);
-
-  // All of this warp's weights in flight: groups warp, warp+4, ... (u-th).
-  const int ng = (G - warp + kGemvWarps - 1) / kGemvWarps;  // groups of this warp
-  float sca[kCpaMaxGroupsPerWarp], scb[kCpaMaxGroupsPerWarp];
-#pragma unroll
-  for (int u = 0; u < kCpaMaxGroupsPerWarp; ++u) {
-    if (u < ng) {
-      const int grp = warp + kGemvWarps * u;
-      const int off = grp * kGroupBytes + tq * 16;
-      cp_async16(wbuf + (u * 2 + 0) * 512 + lane * 16, qa + off);
-      cp_async16(wbuf + (u * 2 + 1) * 512 + lane * 16, qb + off);
-      cp_async_commit();
-      sca[u] = bf16_bits_to_f32(ldg_u16(sa_p + grp));
-      scb[u] = bf16_bits_to_f32(ldg_u16(sb_p + grp));
-    }
-  }
-  if (MODE == ROW_DENSE) pdl_wait();
-  {
-    const int nwords = in / 8;
-    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
-    for (int wi = threadIdx.x; wi < ((nwords + 127) & ~127); wi += kGemvThreads) {
-      float part = 0.f;
-      if (wi < nwords) {
-        const uint4 v = __ldg(xv + wi);
-        uint4 o;
-        o.x = __byte_perm(v.x, v.z, 0x5410);
-        o.y = __byte_perm(v.x, v.z, 0x7632);
-        o.z = __byte_perm(v.y, v.w, 0x5410);
-        o.w = __byte_perm(v.y, v.w, 0x7632);
-        const int grp = wi >> 4, t = (wi >> 2) & 3, w = wi & 3;
-        *reinterpret_cast<uint4*>(xs + xperm_word(grp, t) + 4 * w) = o;
-        part = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) +
-               bf16_bits_to_f32(v.y & 0xFFFF) + bf16_bits_to_f32(v.y >> 16) +
-               bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
-               bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
-      }
-      part += __shfl_xor_sync(0xffffffffu, part, 8);
-      part += __shfl_xor_sync(0xffffffffu, part, 4);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
-    }
-  }
-  __syncthreads();
-
-  float acc_a = 0.f, acc_b = 0.f;
-#pragma unroll
-  for (int u = 0; u < kCpaMaxGroupsPerWarp; ++u) {
-    if (u < ng) {
-      const int grp = warp + kGemvWarps * u;
-      cp_async_wait(ng - 1 - u);
-      const uint4 wa = *reinterpret_cast<const uint4*>(wbuf + (u * 2 + 0) * 512 + lane * 16);
-      const uint4 wb = *reinterpret_cast<const uint4*>(wbuf + (u * 2 + 1) * 512 + lane * 16);
-      const uint4* bp = reinterpret_cast<const uint4*>(xs + xperm_word(grp, tq));
-      const uint4 b01 = bp[0], b23 = bp[1], b45 = bp[2], b67 = bp[3];
-      const uint32_t bw[16] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w,
-                               b45.x, b45.y, b45.z, b45.w, b67.x, b67.y, b67.z, b67.w};
-      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-      group_mma(wa, wb, bw, d0, d1);
-      const float bias = kNibbleBias * gsum[grp];
-      acc_a = fmaf(sca[u], (d0[0] + d1[0]) - bias, acc_a);
-      acc_b = fmaf(scb[u], (d0[2] + d1[2]) - bias, acc_b);
-    }
-  }
-  pdl_launch_dependents();
-  if (tq == 0) {
-    red[warp * 16 + gq] = acc_a;
-    red[warp * 16 + gq + 8] = acc_b;
-  }
-  __syncthreads();
-  if (threadIdx.x < 16) {
-    const int j = tile0 + threadIdx.x;
-    if (j < n_out) {
-      float v = red[threadIdx.x];
-#pragma unroll
-      for (int w = 1; w < kGemvWarps; ++w) v += red[w * 16 + threadIdx.x];
-      const bool ok = (threadIdx.x < 8) ? oka : okb;
-      uint16_t o;
-      if (!ok) {
-        o = 0;
-      } else if (EPI == EPI_PLAIN) {
-        o = f32_to_bf16_bits(v);
-      } else if (EPI == EPI_SILU) {
-        o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
-        hist_count(p.hist, o);
-      } else {
-        o = f32_to_bf16_bits(bf16_bits_to_f32(p.g[p.gid[j]]) * round_bf16(v));
-      }
-      p.out[j] = o;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Persistent pipelined variant (default when in_features % 1024 == 0).
-// One CTA of 16 warps per SM walks a contiguous range of 16-row tiles as two
-// warp groups of 8 that take alternate tiles.  In a warp group, warp w owns
-// the K-slice of groups [w*GW, (w+1)*GW).  Every thread keeps the next tile
-// of its own weight bytes in flight with cp.async (a commit group per tile),
-// so HBM requests continue while the tensor cores work; with 16 warps per SM
-// four warps per scheduler hide the MMA and shared-memory latencies.  Per
-// tile: wait, group barrier (the tile's scale rows were copied by other
-// threads of the group), MMA, fixed-order combine of the 8 K-slices.  The
-// row pointers and the epilogue's per-row data (validity, g[channel]) are
-// resolved once in the prologue so no global load sits on the per-tile path.
-constexpr int kPipeGroupWarps = 8;
-constexpr int kPipeWarps = 2 * kPipeGroupWarps;
-constexpr int kPipeThreads = kPipeWarps * 32;
-constexpr int kPipeDepth = 2;  // tiles per warp group in flight (incl. current)
+// Default variant: persistent K-slice streaming, no per-tile synchronisation.
+//
+// One CTA of 8 warps per SM takes a contiguous range of 16-row tiles.  Warp w
+// owns the K-slice of quantisation groups [w*GW, (w+1)*GW) for EVERY tile of
+// the CTA, so its x fragments and group sums live in registers for the whole
+// kernel and the work of an SM is split evenly between its warps.  Each warp
+// streams its slice of each tile (16 rows x GW x 64 B) plus the covering
+// 32 bytes of the 16 scale rows through a private 4-deep shared-memory ring
+// with 16-byte cp.async.cg copies and never waits for another warp: its
+// per-tile partial sums go to shared memory, and the 8 slices of every row
+// are combined, in a fixed order, once after a single barrier at the end.
+// (Measured on B200: rolling per-warp cp.async pipelines stream at ~6.4 TB/s
+// with ~40 KB in flight per SM; the same GEMV with a block barrier per tile
+// stalled at 2.5-3 TB/s, and 8-row whole-K tiles per warp at ~2 TB/s because
+// of x-fragment reloads and uneven warp loads.)
+constexpr int kKsWarps = 8;
+constexpr int kKsThreads = kKsWarps * 32;
+constexpr int kKsDepth = 4;
 
-struct PipeGeom {
-  int gw, wslot, scb, sc_slot, ring_off, sc_off, ptr_off, info_off, x_off, gsum_off, red_off,
-      total;
+struct KsGeom {
+  int gw, slot, w_bytes, ring_off, ptr_off, info_off, red_off, x_off, gsum_off, total;
 };
-__host__ __device__ inline PipeGeom pipe_geom(int in, int max_tiles) {
-  PipeGeom g;
+__host__ __device__ inline KsGeom ks_geom(int in, int max_tiles) {
+  KsGeom g;
   const int G = in / kGroup;
-  g.gw = G / kPipeGroupWarps;
-  g.wslot = g.gw * 1024;  // per warp per tile: GW groups x 2 rows x 512 B
-  g.scb = G * 2;
-  g.sc_slot = 16 * g.scb;
+  g.gw = G / kKsWarps;
+  g.w_bytes = g.gw * 1024;            // 16 rows x GW x 64 B
+  g.slot = g.w_bytes + 16 * 32;       // + 32 bytes of each of the 16 scale rows
   g.ring_off = 0;
-  g.sc_off = kPipeWarps * kPipeDepth * g.wslot;
-  g.ptr_off = g.sc_off + 2 * kPipeDepth * g.sc_slot;
-  g.info_off = g.ptr_off + max_tiles * 16 * 16;  // (qw, sc) pointers per row
-  g.x_off = g.info_off + max_tiles * 16 * 4;     // per-row epilogue value
+  g.ptr_off = kKsWarps * kKsDepth * g.slot;
+  g.info_off = g.ptr_off + max_tiles * 16 * 16;
+  g.red_off = g.info_off + max_tiles * 16 * 4;
+  g.x_off = g.red_off + max_tiles * kKsWarps * 16 * 4;
   g.gsum_off = g.x_off + G * 72 * 4;
-  g.red_off = g.gsum_off + ((G * 4 + 15) & ~15);
-  g.total = g.red_off + 2 * 2 * kPipeGroupWarps * 16 * 4;
+  g.total = g.gsum_off + ((G * 4 + 15) & ~15);
   return g;
 }
 
 template <int MODE, int EPI, int GW>
-__global__ void __launch_bounds__(kPipeThreads, 1)
-gemv_pipe_kernel(const GemvParams p, int max_tiles) {
+__global__ void __launch_bounds__(kKsThreads, 1)
+gemv_ks_kernel(const GemvParams p, int max_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int in = p.in_features;
   const int G = in / kGroup;
-  const PipeGeom geo = pipe_geom(in, max_tiles);
+  const KsGeom geo = ks_geom(in, max_tiles);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wg = warp / kPipeGroupWarps, kw = warp % kPipeGroupWarps, gtid = tid % 256;
   const int gq = lane >> 2, tq = lane & 3;
   const uint8_t** rq = reinterpret_cast<const uint8_t**>(smem + geo.ptr_off);
   const uint16_t** rs = reinterpret_cast<const uint16_t**>(smem + geo.ptr_off) + max_tiles * 16;
   float* info = reinterpret_cast<float*>(smem + geo.info_off);  // NaN marks an invalid row
+  float* red = reinterpret_cast<float*>(smem + geo.red_off);    // [tile][warp][16]
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + geo.x_off);
   float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
-  float* red = reinterpret_cast<float*>(smem + geo.red_off) + wg * 2 * kPipeGroupWarps * 16;
+  uint8_t* ring = smem + geo.ring_off + warp * kKsDepth * geo.slot;
 
   if (MODE != ROW_DENSE) pdl_wait();
   int n_out = p.n_out;
@@ -485,7 +352,7 @@ gemv_pipe_kernel(const GemvParams p, int max_tiles) {
   const int t0 = (int)((int64_t)nt * blockIdx.x / gridDim.x);
   const int t1 = (int)((int64_t)nt * (blockIdx.x + 1) / gridDim.x);
   const int ntile = t1 - t0;
-  for (int r = tid; r < ntile * 16; r += kPipeThreads) {
+  for (int r = tid; r < ntile * 16; r += kKsThreads) {
     const int j = min(t0 * 16 + r, n_out - 1);
     const uint8_t* qw;
     const uint16_t* sc;
@@ -498,39 +365,37 @@ gemv_pipe_kernel(const GemvParams p, int max_tiles) {
   }
   __syncthreads();
 
-  // This warp group's tiles: local tiles wg, wg+2, ...; n_mine of them.
-  const int n_mine = (ntile - wg + 1) / 2;
-  const int nsc_chunks = 16 * geo.scb / 16;
-  const int sc_per_row = geo.scb / 16;
-  auto issue = [&](int m) {  // m-th tile of this warp group
-    if (m < n_mine) {
-      const int i = wg + 2 * m;
-      uint8_t* ws = smem + geo.ring_off + (warp * kPipeDepth + m % kPipeDepth) * geo.wslot;
+  // Scale bytes of this slice: [2*GW*warp, 2*GW*(warp+1)) of each scale row,
+  // covered by the 32 bytes starting at the 16-byte boundary below it.
+  const int sc_lo = (2 * GW * warp) & ~15;
+  const int sc_shift = 2 * GW * warp - sc_lo;  // bytes
+  auto issue = [&](int i) {
+    if (i < ntile) {
+      uint8_t* slot = ring + (i % kKsDepth) * geo.slot;
       const uint8_t* qa = rq[i * 16 + gq];
       const uint8_t* qb = rq[i * 16 + gq + 8];
 #pragma unroll
       for (int gi = 0; gi < GW; ++gi) {
-        const int off = (kw * GW + gi) * kGroupBytes + tq * 16;
-        cp_async16(ws + (gi * 2 + 0) * 512 + lane * 16, qa + off);
-        cp_async16(ws + (gi * 2 + 1) * 512 + lane * 16, qb + off);
+        const int off = (warp * GW + gi) * kGroupBytes + tq * 16;
+        cp_async16(slot + (gi * 2 + 0) * 512 + lane * 16, qa + off);
+        cp_async16(slot + (gi * 2 + 1) * 512 + lane * 16, qb + off);
       }
-      uint8_t* sdst = smem + geo.sc_off + (wg * kPipeDepth + m % kPipeDepth) * geo.sc_slot;
-      for (int c = gtid; c < nsc_chunks; c += 256) {
-        const int row = c / sc_per_row, part = c % sc_per_row;
-        cp_async16(sdst + row * geo.scb + part * 16, rs[i * 16 + row] + part * 8);
-      }
+      // lane -> scale row lane/2, 16-byte half lane%2
+      const uint8_t* srow = reinterpret_cast<const uint8_t*>(rs[i * 16 + (lane >> 1)]);
+      const int sofs = sc_lo + (lane & 1) * 16;
+      if (sofs < 2 * G) cp_async16(slot + geo.w_bytes + lane * 16, srow + sofs);
     }
     cp_async_commit();
   };
 #pragma unroll
-  for (int m = 0; m < kPipeDepth - 1; ++m) issue(m);
+  for (int i = 0; i < kKsDepth - 1; ++i) issue(i);
 
   if (MODE == ROW_DENSE) pdl_wait();
   {
     const int nwords = in / 8;
     const uint4* xv = reinterpret_cast<const uint4*>(p.x);
-    for (int wi = tid; wi < ((nwords + kPipeThreads - 1) / kPipeThreads) * kPipeThreads;
-         wi += kPipeThreads) {
+    for (int wi = tid; wi < ((nwords + kKsThreads - 1) / kKsThreads) * kKsThreads;
+         wi += kKsThreads) {
       float part = 0.f;
       if (wi < nwords) {
         const uint4 v = __ldg(xv + wi);
@@ -554,126 +419,115 @@ gemv_pipe_kernel(const GemvParams p, int max_tiles) {
     }
   }
   __syncthreads();
+  uint32_t xf[GW][16];
   float bias[GW];
 #pragma unroll
-  for (int gi = 0; gi < GW; ++gi) bias[gi] = kNibbleBias * gsum[kw * GW + gi];
+  for (int gi = 0; gi < GW; ++gi) {
+    const int grp = warp * GW + gi;
+    const uint4* bp = reinterpret_cast<const uint4*>(xs + xperm_word(grp, tq));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 b = bp[q];
+      xf[gi][4 * q + 0] = b.x; xf[gi][4 * q + 1] = b.y;
+      xf[gi][4 * q + 2] = b.z; xf[gi][4 * q + 3] = b.w;
+    }
+    bias[gi] = kNibbleBias * gsum[grp];
+  }
 
-  for (int m = 0; m < n_mine; ++m) {
-    issue(m + kPipeDepth - 1);
-    cp_async_wait(kPipeDepth - 1);
-    named_bar(1 + wg, 256);  // scale rows of this tile (other threads' copies) visible
-    const int i = wg + 2 * m;
-    const uint8_t* ws = smem + geo.ring_off + (warp * kPipeDepth + m % kPipeDepth) * geo.wslot;
-    const uint8_t* sbase = smem + geo.sc_off + (wg * kPipeDepth + m % kPipeDepth) * geo.sc_slot;
-    const uint16_t* sca = reinterpret_cast<const uint16_t*>(sbase + gq * geo.scb);
-    const uint16_t* scbp = reinterpret_cast<const uint16_t*>(sbase + (gq + 8) * geo.scb);
+  for (int i = 0; i < ntile; ++i) {
+    issue(i + kKsDepth - 1);
+    cp_async_wait(kKsDepth - 1);
+    __syncwarp();  // scale bytes were copied by other lanes of this warp
+    const uint8_t* slot = ring + (i % kKsDepth) * geo.slot;
+    const uint16_t* sca =
+        reinterpret_cast<const uint16_t*>(slot + geo.w_bytes + gq * 32 + sc_shift);
+    const uint16_t* scb =
+        reinterpret_cast<const uint16_t*>(slot + geo.w_bytes + (gq + 8) * 32 + sc_shift);
     float acc_a = 0.f, acc_b = 0.f;
 #pragma unroll
     for (int gi = 0; gi < GW; ++gi) {
-      const int grp = kw * GW + gi;
-      const uint4 wa = *reinterpret_cast<const uint4*>(ws + (gi * 2 + 0) * 512 + lane * 16);
-      const uint4 wb = *reinterpret_cast<const uint4*>(ws + (gi * 2 + 1) * 512 + lane * 16);
-      const uint4* bp = reinterpret_cast<const uint4*>(xs + xperm_word(grp, tq));
-      const uint4 b01 = bp[0], b23 = bp[1], b45 = bp[2], b67 = bp[3];
-      const uint32_t bw[16] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w,
-                               b45.x, b45.y, b45.z, b45.w, b67.x, b67.y, b67.z, b67.w};
+      const uint4 wa = *reinterpret_cast<const uint4*>(slot + (gi * 2 + 0) * 512 + lane * 16);
+      const uint4 wb = *reinterpret_cast<const uint4*>(slot + (gi * 2 + 1) * 512 + lane * 16);
       float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-      group_mma(wa, wb, bw, d0, d1);
-      acc_a = fmaf(bf16_bits_to_f32(sca[grp]), (d0[0] + d1[0]) - bias[gi], acc_a);
-      acc_b = fmaf(bf16_bits_to_f32(scbp[grp]), (d0[2] + d1[2]) - bias[gi], acc_b);
+      group_mma(wa, wb, xf[gi], d0, d1);
+      acc_a = fmaf(bf16_bits_to_f32(sca[gi]), (d0[0] + d1[0]) - bias[gi], acc_a);
+      acc_b = fmaf(bf16_bits_to_f32(scb[gi]), (d0[2] + d1[2]) - bias[gi], acc_b);
     }
-    float* rr = red + (m & 1) * kPipeGroupWarps * 16;
     if (tq == 0) {
-      rr[kw * 16 + gq] = acc_a;
-      rr[kw * 16 + gq + 8] = acc_b;
+      red[(i * kKsWarps + warp) * 16 + gq] = acc_a;
+      red[(i * kKsWarps + warp) * 16 + gq + 8] = acc_b;
     }
-    named_bar(1 + wg, 256);
-    if (kw == 0 && lane < 16) {
-      const int j = (t0 + i) * 16 + lane;
-      if (j < n_out) {
-        float v = rr[lane];
-#pragma unroll
-        for (int w = 1; w < kPipeGroupWarps; ++w) v += rr[w * 16 + lane];
-        const float inf = info[i * 16 + lane];
-        uint16_t o;
-        if (inf != inf) {
-          o = 0;  // invalid row index
-        } else if (EPI == EPI_PLAIN) {
-          o = f32_to_bf16_bits(v);
-        } else if (EPI == EPI_SILU) {
-          o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
-          hist_count(p.hist, o);
-        } else {
-          o = f32_to_bf16_bits(inf * round_bf16(v));
-        }
-        p.out[j] = o;
-      }
-    }
+    __syncwarp();  // the slot is refilled by a later iteration's copies
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   pdl_launch_dependents();
+  __syncthreads();
+  for (int r = tid; r < ntile * 16; r += kKsThreads) {
+    const int j = t0 * 16 + r;
+    if (j >= n_out) continue;
+    const int i = r >> 4, row = r & 15;
+    float v = red[(i * kKsWarps) * 16 + row];
+#pragma unroll
+    for (int w = 1; w < kKsWarps; ++w) v += red[(i * kKsWarps + w) * 16 + row];
+    const float inf = info[r];
+    uint16_t o;
+    if (inf != inf) {
+      o = 0;  // invalid row index
+    } else if (EPI == EPI_PLAIN) {
+      o = f32_to_bf16_bits(v);
+    } else if (EPI == EPI_SILU) {
+      o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
+      hist_count(p.hist, o);
+    } else {
+      o = f32_to_bf16_bits(inf * round_bf16(v));
+    }
+    p.out[j] = o;
+  }
 }
 
 template <int MODE, int EPI, int GW>
-static int launch_pipe(const GemvParams& p, cudaStream_t s) {
+static int launch_ks(const GemvParams& p, cudaStream_t s) {
   const int nt = (p.n_out + 15) / 16;
   const int grid = nt < num_sms() ? nt : num_sms();
   const int max_tiles = (nt + grid - 1) / grid;
-  const PipeGeom geo = pipe_geom(p.in_features, max_tiles);
-  auto kern = gemv_pipe_kernel<MODE, EPI, GW>;
+  const KsGeom geo = ks_geom(p.in_features, max_tiles);
+  auto kern = gemv_ks_kernel<MODE, EPI, GW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        geo.total);
   if (e != cudaSuccess) return launch_status(e);
-  return launch_status(launch(kern, dim3(grid), dim3(kPipeThreads), (size_t)geo.total, s, p,
+  return launch_status(launch(kern, dim3(grid), dim3(kKsThreads), (size_t)geo.total, s, p,
                               max_tiles));
 }
 
-static bool pipe_ok(const GemvParams& p) {
+// Needs whole 8-way K slices (G % 8 == 0), 16-byte aligned scale rows and a
+// ring that fits in shared memory.
+static bool ks_ok(const GemvParams& p) {
   const int G = p.in_features / kGroup;
-  if (G % kPipeGroupWarps != 0 || G / kPipeGroupWarps > 6) return false;
+  if (G % kKsWarps != 0 || G / kKsWarps > 6) return false;
   if ((reinterpret_cast<uintptr_t>(p.sc0) & 15) != 0) return false;
   if (p.qw1 && (reinterpret_cast<uintptr_t>(p.sc1) & 15) != 0) return false;
   const int nt = (p.n_out + 15) / 16;
   const int grid = nt < num_sms() ? nt : num_sms();
-  return pipe_geom(p.in_features, (nt + grid - 1) / grid).total <= 225 * 1024;
+  return ks_geom(p.in_features, (nt + grid - 1) / grid).total <= 225 * 1024;
 }
 
 template <int MODE, int EPI>
-static int launch_pipe_any(const GemvParams& p, cudaStream_t s) {
-  switch (p.in_features / kGroup / kPipeGroupWarps) {
-    case 1: return launch_pipe<MODE, EPI, 1>(p, s);
-    case 2: return launch_pipe<MODE, EPI, 2>(p, s);
-    case 3: return launch_pipe<MODE, EPI, 3>(p, s);
-    case 4: return launch_pipe<MODE, EPI, 4>(p, s);
-    case 5: return launch_pipe<MODE, EPI, 5>(p, s);
-    default: return launch_pipe<MODE, EPI, 6>(p, s);
+static int launch_ks_any(const GemvParams& p, cudaStream_t s) {
+  switch (p.in_features / kGroup / kKsWarps) {
+    case 1: return launch_ks<MODE, EPI, 1>(p, s);
+    case 2: return launch_ks<MODE, EPI, 2>(p, s);
+    case 3: return launch_ks<MODE, EPI, 3>(p, s);
+    case 4: return launch_ks<MODE, EPI, 4>(p, s);
+    case 5: return launch_ks<MODE, EPI, 5>(p, s);
+    default: return launch_ks<MODE, EPI, 6>(p, s);
   }
-}
-
-static bool cpa_ok(const GemvParams& p) {
-  const int G = p.in_features / kGroup;
-  return (G + kGemvWarps - 1) / kGemvWarps <= kCpaMaxGroupsPerWarp;
-}
-
-template <int MODE, int EPI>
-static int launch_cpa(const GemvParams& p, cudaStream_t s) {
-  const CpaGeom geo = cpa_geom(p.in_features);
-  auto kern = gemv_cpa_kernel<MODE, EPI>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       geo.total);
-  if (e != cudaSuccess) return launch_status(e);
-  const dim3 grid((p.n_out + 15) / 16);
-  return launch_status(launch(kern, grid, dim3(kGemvThreads), (size_t)geo.total, s, p));
 }
 
 // Host launcher shared by the entry points below.
 template <int MODE, int EPI>
 static int launch_gemv(const GemvParams& p, cudaStream_t s) {
   if (p.n_out == 0) return DIP_OK;
-  if (!force_simple_gemv()) {
-    if (pipe_ok(p)) return launch_pipe_any<MODE, EPI>(p, s);
-    if (cpa_ok(p)) return launch_cpa<MODE, EPI>(p, s);
-  }
+  if (!force_simple_gemv() && ks_ok(p)) return launch_ks_any<MODE, EPI>(p, s);
   const int G = p.in_features / kGroup;
   const size_t smem = (size_t)p.in_features * 2 + (size_t)G * 4 + kGemvWarps * 16 * 4;
   auto kern = gemv_int4_kernel<MODE, EPI>;
