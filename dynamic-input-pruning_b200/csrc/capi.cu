@@ -83,7 +83,7 @@ extern "C" int dip_take_device_error(unsigned int* out) {
 
 extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k < 0) return 0;
-  return align256(topk_scratch_bytes()) + align256((size_t)inter * 2) + align256((size_t)k * 4) +
+  return align256(topk_scratch_bytes()) + 256 + align256((size_t)inter * 2) + align256((size_t)k * 4) +
          align256((size_t)k * 2) + align256(down_workspace_bytes(hidden));
 }
 
@@ -98,6 +98,8 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   unsigned* hist = reinterpret_cast<unsigned*>(ws);
   ws += align256(topk_scratch_bytes());
+  GridBar* bars = reinterpret_cast<GridBar*>(ws);  // stays valid across calls
+  ws += 256;
   dip_bf16* g = reinterpret_cast<dip_bf16*>(ws);
   ws += align256((size_t)L->inter * 2);
   int32_t* idx = reinterpret_cast<int32_t*>(ws);
@@ -117,5 +119,6 @@ extern "C" int dip_mlp_decode(const dip_layer_t* L, const dip_bf16* x, int64_t k
   st = dip_gather_up_h(L->up_qw, L->up_sc, L->inter, x, g, idx, k, L->hidden, h, stream);
   if (st) return st;
   return gather_down_clear(L->down_t_qw, L->down_t_sc, L->inter, h, idx, k, L->hidden, part,
-                           part_bytes, y, hist, topk_scratch_bytes(), (cudaStream_t)stream);
+                           part_bytes, y, hist, topk_scratch_bytes(), &bars[0],
+                           (cudaStream_t)stream);
 }

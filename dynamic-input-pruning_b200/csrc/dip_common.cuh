@@ -118,7 +118,33 @@ cudaError_t launch(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// As launch(), additionally asking for a cooperative launch (all CTAs
+// resident at once; the launch fails instead of running otherwise).
+template <typename Kernel, typename... Args>
+cudaError_t launch_coop(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                        Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 int num_sms();
+
+// Words of a grid-wide barrier (see grid_sync).
+struct GridBar {
+  unsigned count;
+  unsigned gen;
+};
 
 // Test switch: route the GEMV family through the simple (non-ring) kernel.
 bool force_simple_gemv();
@@ -142,7 +168,7 @@ int topk_compact_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, u
 int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_rows,
                       const uint16_t* h, const int32_t* idx, int64_t k, int64_t out_features,
                       void* workspace, size_t workspace_bytes, uint16_t* y, void* clear,
-                      size_t clear_bytes, cudaStream_t stream);
+                      size_t clear_bytes, GridBar* bar, cudaStream_t stream);
 
 }  // namespace dip
 
@@ -199,6 +225,37 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Grid-wide barrier (declared above) for a grid whose CTAs are all resident at once (one CTA
+// per SM, grid <= SM count, launched cooperatively).  Sense-reversing: the
+// last CTA to arrive resets the count and advances the generation, so the two
+// words can be reused by any later launch, whatever its grid size; they must
+// be zero before the first use.  The wait is bounded: on timeout the error
+// word is flagged and the CTA continues (its results are then invalid).
+__device__ __forceinline__ void grid_sync(GridBar* b, unsigned* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned g0;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g0) : "l"(&b->gen) : "memory");
+    __threadfence();
+    const unsigned nb = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(&b->count, 1u) == nb - 1) {
+      atomicExch(&b->count, 0u);
+      __threadfence();
+      atomicAdd(&b->gen, 1u);
+    } else {
+      bool done = false;
+      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+        unsigned g;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(&b->gen) : "memory");
+        done = (g != g0);
+      }
+      if (!done) atomicOr(err, kErrTimeout);
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
 // Named barrier for a subset of warps (id 1..15).
 __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");

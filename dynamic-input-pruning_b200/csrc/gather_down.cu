@@ -34,6 +34,10 @@ struct DownParams {
   const int32_t* count;   // optional device-side number of rows (<= k)
   uint4* clear;           // optional: zeroed by the reduction kernel
   int clear_n16;
+  GridBar* bar;           // fused reduction: grid barrier words (zero on first use)
+  unsigned* err;
+  uint16_t* y;            // fused reduction outputs
+  float* y_f32;
   int k;
   int out_features;
 };
@@ -236,7 +240,7 @@ __host__ __device__ inline DmGeom dm_geom(int nwarps, int max_slice) {
   return g;
 }
 
-template <int MODE>
+template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(640, 1)
 down_mma_kernel(const DownParams p, int max_slice) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -368,6 +372,30 @@ down_mma_kernel(const DownParams p, int max_slice) {
       reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
                                                       v[4 * q + 3]);
   }
+  if (FUSED) {
+    // All partial vectors written -> every CTA sums a slice of the outputs
+    // over the slices in a fixed order (8 threads per output, fixed tree).
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.clear_n16;
+         i += gridDim.x * blockDim.x)
+      p.clear[i] = make_uint4(0, 0, 0, 0);
+    grid_sync(p.bar, p.err);
+    const int per = (out + gridDim.x - 1) / gridDim.x;
+    const int o0 = blockIdx.x * per;
+    const int oi = threadIdx.x >> 3, part = threadIdx.x & 7;
+    for (int ob = 0; ob < per; ob += blockDim.x >> 3) {
+      const int o = o0 + ob + oi;
+      float acc = 0.f;
+      if (ob + oi < per && o < out)
+        for (int c = part; c < nslices; c += 8) acc += p.partial[(size_t)c * out + o];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      if (part == 0 && ob + oi < per && o < out) {
+        if (p.y) p.y[o] = f32_to_bf16_bits(acc);
+        if (p.y_f32) p.y_f32[o] = acc;
+      }
+    }
+  }
 }
 
 static bool dm_ok(const DownParams& p) {
@@ -393,7 +421,17 @@ int launch_down(DownParams p, uint16_t* y, float* y_f32, void* ws, size_t ws_byt
     const int max_slice = (p.k + nsl - 1) / nsl + 1;
     const DmGeom geo = dm_geom(out / 256, max_slice);
     if (geo.total <= 220 * 1024) {
-      auto kern = down_mma_kernel<MODE>;
+      if (p.bar && 2 * nsl <= num_sms()) {
+        auto kf = down_mma_kernel<MODE, true>;
+        cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             geo.total);
+        if (e != cudaSuccess) return launch_status(e);
+        p.y = y;
+        p.y_f32 = y_f32;
+        return launch_status(launch_coop(kf, dim3(2 * nsl), dim3(out / 256 * 32),
+                                         (size_t)geo.total, st, p, max_slice));
+      }
+      auto kern = down_mma_kernel<MODE, false>;
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            geo.total);
       if (e != cudaSuccess) return launch_status(e);
@@ -559,7 +597,7 @@ namespace dip {
 int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_rows,
                       const uint16_t* h, const int32_t* idx, int64_t k, int64_t out_features,
                       void* workspace, size_t workspace_bytes, uint16_t* y, void* clear,
-                      size_t clear_bytes, cudaStream_t stream) {
+                      size_t clear_bytes, GridBar* bar, cudaStream_t stream) {
   if (k <= 0 || k > INT32_MAX || n_rows <= 0 || !down_shape_ok(out_features) || !y || !down_t ||
       !scales || !h || !idx || !al16(down_t) || (clear_bytes % 16) != 0)
     return DIP_ERR_ARG;
@@ -571,6 +609,9 @@ int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_ro
   p.idx = idx;
   p.clear = static_cast<uint4*>(clear);
   p.clear_n16 = (int)(clear_bytes / 16);
+  p.bar = bar;
+  p.err = error_word_ptr();
+  if (bar && !p.err) return DIP_ERR_CUDA;
   p.k = (int)k;
   p.out_features = (int)out_features;
   return launch_down<DROW_GATHER>(p, y, nullptr, workspace, workspace_bytes, stream);
