@@ -164,7 +164,7 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     cfg = StackConfig(n_layers=args.layers, seed=rank)
-    stack = DipStack(cfg, dev)
+    stack = DipStack(cfg, dev, fused=(args.path == "fused"))
     T = args.warmup + args.steps
     x0, resid = token_inputs(cfg, T, seed=1000 + rank, device=dev)
     stack.capture()
@@ -256,7 +256,8 @@ def run_ours(args):
                      "traffic": traffic, "algorithmic_bytes": nb["gate"],
                      "avg_launch_us": gate_avg * 1e3},
         "e2e": e2e,
-        "gpu_launches": args.steps * (cfg.n_layers * 5 + cfg.n_layers - 1),
+        "gpu_launches": args.steps * (cfg.n_layers if stack.fused else cfg.n_layers * 6 - 1),
+        "path": args.path,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -283,6 +284,8 @@ def main():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--cpu-layers", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="fused", choices=["fused", "chain"],
+                    help="fused: one persistent kernel per layer; chain: separate launches")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

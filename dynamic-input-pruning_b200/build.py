@@ -25,7 +25,7 @@ LIBDIR = PKG_ROOT / "dip_b200" / "_lib"
 INCLUDE = REPO / "include"
 
 CORE_SOURCES = ["capi.cu", "gemv_int4.cu", "topk.cu", "gather_down.cu", "quant.cu",
-                "stack_ops.cu"]
+                "stack_ops.cu", "layer_fused.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -51,7 +51,7 @@ def build_core(force: bool = False) -> Path:
     LIBDIR.mkdir(parents=True, exist_ok=True)
     out = LIBDIR / "libdip_core.so"
     srcs = [CSRC / s for s in CORE_SOURCES]
-    deps = srcs + [CSRC / "dip_common.cuh", INCLUDE / "dip_b200.h"]
+    deps = srcs + [CSRC / "dip_common.cuh", CSRC / "dip_block.cuh", INCLUDE / "dip_b200.h"]
     if not force and not _stale(out, deps):
         return out
     objdir = PKG_ROOT / "_build"

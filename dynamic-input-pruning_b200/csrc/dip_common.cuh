@@ -141,10 +141,15 @@ cudaError_t launch_coop(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream
 int num_sms();
 
 // Words of a grid-wide barrier (see grid_sync).
+// The arrival counter and the generation word sit on separate 128-byte lines
+// so that the CTAs polling the generation do not contend with the arrivals.
 struct GridBar {
   unsigned count;
+  unsigned pad0[31];
   unsigned gen;
+  unsigned pad1[31];
 };
+static_assert(sizeof(GridBar) == 256, "grid barrier words occupy 256 bytes of workspace");
 
 // Test switch: route the GEMV family through the simple (non-ring) kernel.
 bool force_simple_gemv();
@@ -246,9 +251,10 @@ __device__ __forceinline__ void grid_sync(GridBar* b, unsigned* err) {
       bool done = false;
       for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
         unsigned g;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(&b->gen) : "memory");
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(&b->gen) : "memory");
         done = (g != g0);
       }
+      asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
       if (!done) atomicOr(err, kErrTimeout);
     }
     __threadfence();

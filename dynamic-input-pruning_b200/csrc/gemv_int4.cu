@@ -345,6 +345,11 @@ gemv_ks_kernel(const GemvParams p, int max_tiles) {
   float* gsum = reinterpret_cast<float*>(smem + geo.gsum_off);
   uint8_t* ring = smem + geo.ring_off + warp * kKsDepth * geo.slot;
 
+  // |g| histogram: fine bins straight to global memory (spread out), coarse
+  // bins (one per exponent, a handful of them hot) aggregated per CTA first.
+  __shared__ unsigned s_coarse[(EPI == EPI_SILU) ? 256 : 1];
+  if (EPI == EPI_SILU)
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_coarse[i] = 0u;
   if (MODE != ROW_DENSE) pdl_wait();
   int n_out = p.n_out;
   if (p.count) n_out = min(n_out, *p.count);
@@ -477,11 +482,20 @@ gemv_ks_kernel(const GemvParams p, int max_tiles) {
       o = f32_to_bf16_bits(v);
     } else if (EPI == EPI_SILU) {
       o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
-      hist_count(p.hist, o);
+      const unsigned key = o & 0x7FFFu;
+      if (p.hist && key <= 0x7F80u) {
+        atomicAdd(&p.hist[key], 1u);
+        atomicAdd(&s_coarse[key >> 7], 1u);
+      }
     } else {
       o = f32_to_bf16_bits(inf * round_bf16(v));
     }
     p.out[j] = o;
+  }
+  if (EPI == EPI_SILU && p.hist) {
+    __syncthreads();
+    for (int i = tid; i < 256; i += kKsThreads)
+      if (s_coarse[i]) atomicAdd(&p.hist[kTopkHistBins + i], s_coarse[i]);
   }
 }
 

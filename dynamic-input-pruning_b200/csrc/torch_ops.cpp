@@ -408,6 +408,45 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
   return y;
 }
 
+std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
+    const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
+    const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
+    double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
+  check_packed(gate_qw, gate_sc, "mlp_decode_fused(gate)");
+  check_packed(up_qw, up_sc, "mlp_decode_fused(up)");
+  check_packed(dt_qw, dt_sc, "mlp_decode_fused(down_t)");
+  c10::cuda::CUDAGuard guard(gate_qw.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  const int64_t hidden = gate_qw.size(1) * 2, inter = gate_qw.size(0);
+  TORCH_CHECK(x.numel() == hidden && up_qw.sizes() == gate_qw.sizes() &&
+                  dt_qw.size(0) == inter && dt_qw.size(1) * 2 == hidden,
+              "mlp_decode_fused: shape mismatch");
+  Tensor r;
+  if (resid.has_value()) {
+    r = resid->contiguous();
+    check_dtype(r, at::kBFloat16, "resid");
+    TORCH_CHECK(r.numel() == hidden, "mlp_decode_fused: resid size");
+  }
+  dip_layer_t L = {i8(gate_qw), bf(gate_sc), i8(up_qw), bf(up_sc), i8(dt_qw), bf(dt_sc),
+                   hidden, inter};
+  Tensor y = bf16_empty(hidden, x), g = bf16_empty(inter, x);
+  Tensor idx = at::empty({k}, x.options().dtype(at::kInt));
+  const size_t wsb = dip_mlp_fused_workspace_bytes(hidden, inter, k);
+  Tensor ws = ws_opt.has_value() ? *ws_opt : at::zeros({(int64_t)wsb}, x.options().dtype(at::kByte));
+  TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && (size_t)ws.nbytes() >= wsb,
+              "mlp_decode_fused: workspace too small (need ", wsb, " bytes)");
+  check_status(dip_mlp_decode_fused(&L, bf(x), resid.has_value() ? bf(r) : nullptr, (float)eps, k,
+                                    ws.data_ptr(), wsb, bfm(y), bfm(g), idx.data_ptr<int32_t>(),
+                                    nullptr, cur_stream()),
+               "mlp_decode_fused");
+  return {y, g, idx};
+}
+
+int64_t op_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
+  return (int64_t)dip_mlp_fused_workspace_bytes(hidden, inter, k);
+}
+
 int64_t op_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   return (int64_t)dip_mlp_workspace_bytes(hidden, inter, k);
 }
@@ -461,6 +500,11 @@ TORCH_LIBRARY(dip_b200, m) {
       "mlp_decode(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, Tensor down_t_qw, "
       "Tensor down_t_sc, Tensor x, int k, Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
   m.def("mlp_workspace_bytes(int hidden, int inter, int k) -> int");
+  m.def(
+      "mlp_decode_fused(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
+      "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
+      "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
+  m.def("mlp_fused_workspace_bytes(int hidden, int inter, int k) -> int");
   m.def("quantize_int4(Tensor w) -> (Tensor, Tensor)");
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
@@ -485,6 +529,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("srcrow_up_h", &srcrow_up_h);
   m.impl("srcrow_down", &srcrow_down);
   m.impl("mlp_decode", &mlp_decode);
+  m.impl("mlp_decode_fused", &mlp_decode_fused);
   m.impl("quantize_int4", &quantize_int4);
   m.impl("dequantize_int4", &dequantize_int4);
   m.impl("transpose_down_int4", &transpose_down_int4);
@@ -496,6 +541,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
 TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) {
   m.impl("set_pdl", &op_set_pdl);
   m.impl("mlp_workspace_bytes", &op_mlp_workspace_bytes);
+  m.impl("mlp_fused_workspace_bytes", &op_mlp_fused_workspace_bytes);
   m.impl("set_gemv_variant", &op_set_gemv_variant);
   m.impl("take_device_error", &op_take_device_error);
 }

@@ -48,6 +48,7 @@ def load_ops() -> None:
     core()  # resolve libdip_core first (rpath also finds it)
     torch.ops.load_library(str(OPS_SO))
     _register_fakes()
+    _register_fakes_fused()
     _ops_loaded = True
 
 
@@ -95,6 +96,14 @@ def _register_fakes() -> None:
 
     @rf("dip_b200::mlp_decode")
     def _(gq, gs, uq, us, dq, ds, x, k, workspace=None):
+        return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
+                torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
+                torch.empty(k, dtype=torch.int32, device=x.device))
+
+
+def _register_fakes_fused():
+    @torch.library.register_fake("dip_b200::mlp_decode_fused")
+    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, workspace=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))

@@ -77,8 +77,12 @@ def layer_weight_bytes(cfg: StackConfig) -> dict:
 class DipStack:
     """A stack of resident DIP MLP layers with the synthetic inter-layer step."""
 
-    def __init__(self, cfg: StackConfig, device="cuda:0", layers: list | None = None):
+    def __init__(self, cfg: StackConfig, device="cuda:0", layers: list | None = None,
+                 fused: bool = True):
         self.cfg = cfg
+        # fused: one persistent kernel per layer (dip_mlp_decode_fused, RMSNorm
+        # folded in); otherwise the separate-launch chain (dip_mlp_decode).
+        self.fused = fused
         self.device = torch.device(device)
         self.layers = layers if layers is not None else [
             make_layer(cfg, l, self.device) for l in range(cfg.n_layers)]
@@ -91,20 +95,27 @@ class DipStack:
     # -- one token, eager -------------------------------------------------
     def step(self, x0: torch.Tensor, resid: torch.Tensor, record: bool = False) -> torch.Tensor:
         """x0 [hidden] bf16, resid [n_layers, hidden] bf16 -> last layer's y."""
-        x = x0
         k = self.cfg.k
         if getattr(self, "_ws", None) is None or self._ws.device != x0.device:
-            nb = torch.ops.dip_b200.mlp_workspace_bytes(self.cfg.hidden, self.cfg.inter, k)
-            # zeroed once; every decode call leaves the histogram region zero
+            op = (torch.ops.dip_b200.mlp_fused_workspace_bytes if self.fused
+                  else torch.ops.dip_b200.mlp_workspace_bytes)
+            nb = op(self.cfg.hidden, self.cfg.inter, k)
+            # zeroed once; every decode call leaves it reusable
             self._ws = torch.zeros(nb, dtype=torch.uint8, device=x0.device)
         idxs = []
         y = None
         for l, L in enumerate(self.layers):
-            if l > 0:
-                x = torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
-            y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"], L["up_qw"],
-                                                      L["up_sc"], L["down_t_qw"],
-                                                      L["down_t_sc"], x, k, self._ws)
+            if self.fused:
+                xin, r = (x0, None) if l == 0 else (y, resid[l])
+                y, g, idx = torch.ops.dip_b200.mlp_decode_fused(
+                    L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
+                    L["down_t_sc"], xin, r, RMS_EPS, k, self._ws)
+            else:
+                x = x0 if l == 0 else torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
+                y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"],
+                                                          L["up_qw"], L["up_sc"],
+                                                          L["down_t_qw"], L["down_t_sc"], x, k,
+                                                          self._ws)
             if record:
                 idxs.append(idx)
         if record:

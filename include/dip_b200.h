@@ -195,15 +195,29 @@ DIP_API size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k)
  * top-k histograms, which the gate kernel fills and the last kernel clears); every
  * call leaves that region zero, so a workspace can be reused call after call
  * on one stream. */
-/* The workspace must be ZERO before its first use (its first 130 KB hold the
- * top-k histograms, which the gate kernel fills and the last kernel clears); every
- * call leaves that region zero, so a workspace can be reused call after call
- * on one stream. */
 /* g_out (bf16[inter]) and idx_out (int32[k]) may be NULL; when given they
  * receive the layer's gate activations and selected channels. */
 DIP_API int dip_mlp_decode(const dip_layer_t* layer, const dip_bf16* x, int64_t k, void* workspace,
                    size_t workspace_bytes, dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
                    dip_stream_t stream);
+
+/* ---- a11, one launch: the whole decode layer as one persistent kernel ---------
+ * Same result as dip_mlp_decode (same selection; y within rounding), computed
+ * by one cooperative launch of one CTA per SM: gate GEMV + SiLU + histogram,
+ * grid barrier, top-k thresholds, gathered up and down for the channels each
+ * CTA selected among its own gate rows, grid barrier, fixed-order reduction.
+ * With resid != NULL the layer input is RMSNorm(x + resid) (unit weight, eps),
+ * the inter-layer step of the synthetic stack; x_used (optional) receives the
+ * input used.  The workspace (dip_mlp_fused_workspace_bytes) must be ZERO
+ * before its first use and is left reusable.  Weights, x, g_out and the
+ * workspace must be 16-byte aligned (DIP_ERR_ARG otherwise).  Requires
+ * hidden = 2560 or 5120 (20 warps x 1 or 2 quantisation groups) and at most
+ * 16*12-1 gate rows per SM; otherwise DIP_ERR_UNSUPPORTED. */
+DIP_API size_t dip_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k);
+DIP_API int dip_mlp_decode_fused(const dip_layer_t* layer, const dip_bf16* x,
+                                 const dip_bf16* resid, float eps, int64_t k, void* workspace,
+                                 size_t workspace_bytes, dip_bf16* y, dip_bf16* g_out,
+                                 int32_t* idx_out, dip_bf16* x_used, dip_stream_t stream);
 
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit

@@ -1,0 +1,151 @@
+"""The one-launch persistent layer kernel (dip_mlp_decode_fused) against the
+oracle (GPU): indices bit exact given its g, g / y within the path tolerance,
+deterministic, workspace reusable call after call, RMSNorm-input mode."""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 2e-3
+Y_SCALE_TOL = 4e-4
+
+
+def close(out, ref, scale_tol=0.0):
+    """|out - ref| <= ATOL + RTOL |ref| + scale_tol * max |ref|.
+
+    scale_tol covers y: u is rounded to bf16 from an fp32 sum here and from an
+    fp64 sum in the oracle, so a few channels' h differ by one bf16 ulp and
+    every output carries a random-walk error of ~1e-4 of max |y|; one missing
+    or duplicated channel would move an output by ~1e-2 of max |y|."""
+    out, ref = out.float().cpu(), ref.float().cpu()
+    err = (out - ref).abs()
+    tol = ATOL + RTOL * ref.abs() + scale_tol * ref.abs().max()
+    bad = err > tol
+    if bad.any():
+        i = int((err - tol).argmax())
+        raise AssertionError(f"{int(bad.sum())} out of tolerance, max err {err.max():.3e}; "
+                             f"worst at {i}: got {float(out[i]):.6f}, want {float(ref[i]):.6f}")
+
+
+def _layer(oracle, H, I, seed):
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.ops.dip_b200.quantize_int4
+    w = [(torch.randn(*s, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+         for s in ((I, H), (I, H), (H, I))]
+    gq, gs = q(w[0])
+    uq, us = q(w[1])
+    dq, ds = q(w[2])
+    tq, ts = torch.ops.dip_b200.transpose_down_int4(dq, ds)
+    return {"gate_qw": gq, "gate_sc": gs, "up_qw": uq, "up_sc": us, "down_t_qw": tq,
+            "down_t_sc": ts}
+
+
+def _check(oracle, L, x, k, y, g, idx):
+    cpu = {n: t.cpu() for n, t in L.items()}
+    x = x.cpu()
+    close(g, oracle.silu_bf16(oracle.int4_gemv(cpu["gate_qw"], cpu["gate_sc"], x)))
+    gc = g.cpu()
+    assert torch.equal(idx.cpu(), oracle.topk_select(gc, k))
+    il = idx.cpu().long()
+    u = oracle.int4_gemv(cpu["up_qw"], cpu["up_sc"], x, rows=il)
+    h = (gc[il].float() * u.float()).to(torch.bfloat16)
+    close(y, oracle.gather_down_f32(cpu["down_t_qw"], cpu["down_t_sc"], h, rows=il), Y_SCALE_TOL)
+
+
+@pytest.mark.parametrize("H,I,k", [(5120, 25600, 15360), (2560, 8192, 4915), (5120, 4096, 77)])
+def test_fused_layer_matches_oracle(dip, oracle, H, I, k):
+    L = _layer(oracle, H, I, seed=H + I)
+    x = torch.randn(H, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).cuda()
+    ws = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(H, I, k), dtype=torch.uint8,
+                     device="cuda")
+    args = (L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"], L["down_t_sc"])
+    outs = [torch.ops.dip_b200.mlp_decode_fused(*args, x, None, 1e-6, k, ws) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    for o in outs[1:]:  # deterministic and the workspace is left reusable
+        for a, b in zip(outs[0], o):
+            assert torch.equal(a, b)
+    _check(oracle, L, x, k, *outs[0])
+    # same selection and values as the separate-launch chain, up to rounding
+    y2, g2, idx2 = torch.ops.dip_b200.mlp_decode(*args, x, k)
+    close(outs[0][0], y2, Y_SCALE_TOL)
+
+
+def test_fused_layer_rmsnorm_input(dip, oracle):
+    from dip_b200 import _lib
+    core = _lib.core()
+    H, I, k = 5120, 25600, 15360
+    L = _layer(oracle, H, I, seed=7)
+    gen = torch.Generator().manual_seed(8)
+    yprev = torch.randn(H, generator=gen).to(torch.bfloat16).cuda()
+    r = torch.randn(H, generator=gen).to(torch.bfloat16).cuda()
+
+    class Layer(ctypes.Structure):
+        _fields_ = [(n, ctypes.c_void_p) for n in ("gq", "gs", "uq", "us", "dq", "ds")] + \
+                   [("hidden", ctypes.c_int64), ("inter", ctypes.c_int64)]
+
+    lay = Layer(*(L[n].data_ptr() for n in ("gate_qw", "gate_sc", "up_qw", "up_sc",
+                                             "down_t_qw", "down_t_sc")), H, I)
+    vp = ctypes.c_void_p
+    core.dip_mlp_fused_workspace_bytes.restype = ctypes.c_size_t
+    core.dip_mlp_fused_workspace_bytes.argtypes = [ctypes.c_int64] * 3
+    nws = core.dip_mlp_fused_workspace_bytes(H, I, k)
+    ws = torch.zeros(nws, dtype=torch.uint8, device="cuda")
+    y = torch.empty(H, dtype=torch.bfloat16, device="cuda")
+    g = torch.empty(I, dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty(k, dtype=torch.int32, device="cuda")
+    xu = torch.empty(H, dtype=torch.bfloat16, device="cuda")
+    core.dip_mlp_decode_fused.argtypes = [ctypes.POINTER(Layer), vp, vp, ctypes.c_float,
+                                          ctypes.c_int64, vp, ctypes.c_size_t, vp, vp, vp, vp, vp]
+    st = core.dip_mlp_decode_fused(ctypes.byref(lay), yprev.data_ptr(), r.data_ptr(), 1e-6, k,
+                                   ws.data_ptr(), nws, y.data_ptr(), g.data_ptr(), idx.data_ptr(),
+                                   xu.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    v = yprev.float().cpu() + r.float().cpu()
+    xref = (v * torch.rsqrt(v.square().mean() + 1e-6)).to(torch.bfloat16)
+    close(xu, xref)
+    _check(oracle, L, xu, k, y, g, idx)
+
+
+@pytest.mark.parametrize("case", ["ties", "padding"])
+def test_fused_layer_degenerate_selections(dip, oracle, case):
+    """ties: 50 distinct gate rows repeated over 25600 channels, k inside a tie
+    group, so the tie tier is split across many CTAs in index order.
+    padding: 60% of the gate rows have NaN scales (never selected), fewer
+    valid scores than k, so the index list ends in zeros (channel 0 repeated)."""
+    H, I = 5120, 25600
+    L = _layer(oracle, H, I, seed=11)
+    if case == "ties":
+        k = 15000
+        rep = torch.arange(I, device="cuda") % 50
+        L["gate_qw"] = L["gate_qw"][rep].contiguous()
+        L["gate_sc"] = L["gate_sc"][rep].contiguous()
+    else:
+        k = 15360
+        sc = L["gate_sc"].clone()
+        nan_rows = (torch.arange(I, device="cuda") % 5) >= 2
+        sc[nan_rows] = float("nan")
+        L["gate_sc"] = sc
+    x = torch.randn(H, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    ws = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(H, I, k), dtype=torch.uint8,
+                     device="cuda")
+    args = (L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"], L["down_t_sc"])
+    y, g, idx = torch.ops.dip_b200.mlp_decode_fused(*args, x, None, 1e-6, k, ws)
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    ref_idx = oracle.topk_select(g.cpu(), k)
+    if case == "ties":
+        a = g.float().abs().cpu()
+        w = a[ref_idx.long()].min()
+        n_tie_sel = int((a[ref_idx.long()] == w).sum())
+        assert 0 < n_tie_sel < int((a == w).sum())  # the tie group is split
+    else:
+        assert int((ref_idx == 0).sum()) > 1000  # zero padding
+    _check(oracle, L, x, k, y, g, idx)
+    y2, g2, idx2 = torch.ops.dip_b200.mlp_decode(*args, x, k)
+    assert torch.equal(idx, idx2)
+    close(y, y2, Y_SCALE_TOL)
