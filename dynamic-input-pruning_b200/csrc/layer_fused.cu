@@ -1,17 +1,22 @@
 // layer_fused.cu — one decode DIP MLP layer as ONE persistent kernel.
 //
-//   phase A  gate GEMV + SiLU over this CTA's rows of W_gate; |g| histogram
+// CTA 0 coordinates; CTAs 1..n-1 ("workers") each own a contiguous range of
+// gate rows (= candidate channels):
+//
+//   workers    phase A  gate GEMV + SiLU over the owned rows -> g; coarse |g|
+//                       histogram; arrive (no wait)
+//              spec C   up GEMV of the owned rows with the largest |g| (about
+//                       their expected share of k, nearly always selected),
+//                       started while the selection is computed
+//   CTA 0      waits for every worker's arrival, computes the exact selection
+//              (topk_select.cu semantics) over all of g, publishes thresholds
+//              and each worker's tier counts, releases
+//   workers    take the thresholds, list the owned selected rows, write their
+//              part of idx, up GEMV of the selected rows not yet done, then
+//              the gathered down projection of the selected rows (tensor
+//              cores) into one fp32 partial vector per worker
 //   --- grid barrier ---
-//   phase B  exact top-k thresholds from the histograms (every CTA,
-//            redundantly, ~2 KB of reads); each CTA lists ITS OWN selected
-//            rows: tier A (> hi) is local, tier B (ties) needs the B count
-//            of the rows before its own, read straight from g
-//   phases C+D, one cp.async stream: gathered up GEMV of the listed channels,
-//            h = bf16(g * u) kept in shared memory, then the gathered down
-//            projection of the SAME channels over all outputs (tensor cores),
-//            one fp32 partial vector per CTA
-//   --- grid barrier ---
-//   phase E  fixed-order sum of the partials -> y
+//   all        phase E  fixed-order sum of the partials -> y
 //
 // Semantics are those of StreamingDIPMlp.forward (dip_stream_predispatch.py:
 // 176-204) with topk_select.cu's selection; the kernels of gemv_int4.cu,
@@ -31,21 +36,22 @@
 
 namespace dip {
 
-// Phase tracing (compile with -DDIP_TRACE): CTA 0's thread 0 records the
-// global timer at each phase boundary into dip_lf_trace[].
+// Phase tracing (compile with -DDIP_TRACE): thread 0 of CTA 1 records the
+// global timer at phase boundaries into dip_lf_trace[]; thread 0 of every CTA
+// records its clock at the points of dip_lf_cta[][].
 #ifdef DIP_TRACE
 __device__ unsigned long long dip_lf_trace[16];
-__device__ unsigned long long dip_lf_cta[160][16];
+__device__ unsigned long long dip_lf_cta[160][32];
 }  // namespace dip
 extern "C" void dip_lf_trace_read(unsigned long long* out) {
   cudaMemcpyFromSymbol(out, dip::dip_lf_trace, 16 * sizeof(unsigned long long));
 }
 extern "C" void dip_lf_cta_read(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, dip::dip_lf_cta, 160 * 16 * sizeof(unsigned long long));
+  cudaMemcpyFromSymbol(out, dip::dip_lf_cta, 160 * 32 * sizeof(unsigned long long));
 }
 namespace dip {
 #define LF_TRACE(n) \
-  do { if (threadIdx.x == 0 && blockIdx.x == 0) { unsigned long long t; \
+  do { if (threadIdx.x == 0 && blockIdx.x == 1) { unsigned long long t; \
        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_trace[n] = t; } } while (0)
 #define LF_CTA(n) \
   do { if (threadIdx.x == 0) { dip_lf_cta[blockIdx.x][n] = clock64(); } } while (0)
@@ -71,7 +77,7 @@ struct LfArgs {
   uint16_t* x_used;         // optional: the (normalised) input actually used
   uint16_t* g;              // [inter]
   int32_t* idx;             // [k]
-  unsigned* scratch;        // top-k scratch (zero on entry, left zero)
+  unsigned* scratch;        // selection block (LfSel; zero on entry, left zero)
   float* partial;           // [gridDim.x][hidden]
   uint16_t* y;              // [hidden]
   float* y_f32;             // optional
@@ -80,6 +86,7 @@ struct LfArgs {
 };
 
 // Byte offsets of the dynamic shared memory.
+constexpr int kLfListMax = (kLfTilesA + 1) * 16;  // entries of the C / D lists
 template <int GW>
 struct LfGeom {
   // GEMV phases: 16 rows x GW x 64 B + scale words; down phase: 16 rows at a
@@ -87,21 +94,27 @@ struct LfGeom {
   static constexpr int slot = (GW * 1024 + 64 > 16 * kLfDnPitch + 64) ? GW * 1024 + 64
                                                                        : 16 * kLfDnPitch + 64;
   static constexpr int ring = kLfWarps * kLfDepth * slot;
-  static constexpr int xs = ring;                      // x staging (G*72 words)
+  static constexpr int xs = ring;                      // x staging (G*72 words), phase A start
   static constexpr int G = kLfWarps * GW;
-  static constexpr int gsum = xs + G * 72 * 4;
+  static constexpr int lists = xs;                     // after phase A: rank / C / D lists
+  static constexpr int lists_bytes = 6 * kLfListMax * 4;
+  static constexpr int xs_bytes = (G * 72 * 4 > lists_bytes) ? G * 72 * 4 : lists_bytes;
+  static constexpr int gsum = xs + xs_bytes;
   static constexpr int red = gsum + ((G * 4 + 15) & ~15);  // [tiles][warps][16]
-  static constexpr int red_words = kLfTilesA * kLfWarps * 16;
-  static constexpr int rowp = red + red_words * 4;         // C/D: channel of each list entry
-  static constexpr int hv = rowp + kLfTilesA * 16 * 4;     // C/D: g value, then h (fp32)
-  static constexpr int gloc = hv + kLfTilesA * 16 * 4;     // this CTA's g values (bf16)
-  static constexpr int misc = gloc + kLfTilesA * 16 * 2;   // small scalars
-  static constexpr int total = misc + 1024;
+  static constexpr int red_words = (kLfTilesA + 1) * kLfWarps * 16;
+  static constexpr int gloc = red + red_words * 4;         // this CTA's g values (bf16)
+  static constexpr int misc = gloc + kLfListMax * 2;       // small scalars
+  static constexpr int total = misc + 256;
 };
 
 __device__ __forceinline__ uint16_t ld_cg_u16(const uint16_t* p) {
   unsigned short v;
   asm volatile("ld.global.cg.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned ld_cg_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.global.cg.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
   return v;
 }
 __device__ __forceinline__ int ld_cg_i32(const int32_t* p) {
@@ -120,37 +133,6 @@ __device__ __forceinline__ void cp_async4_lf(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_commit_lf() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_lf() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(kLfDepth - 1) : "memory");
-}
-
-// grid_sync (dip_common.cuh) split in two so that a CTA can do independent
-// work between its arrival and the release.  Thread 0 keeps the generation it
-// saw before arriving; the wait is bounded like grid_sync's.
-__device__ __forceinline__ unsigned lf_bar_arrive(GridBar* b) {
-  __syncthreads();
-  unsigned g0 = 0;
-  if (threadIdx.x == 0) {
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g0) : "l"(&b->gen) : "memory");
-    __threadfence();
-    if (atomicAdd(&b->count, 1u) == gridDim.x - 1) {
-      atomicExch(&b->count, 0u);
-      __threadfence();
-      atomicAdd(&b->gen, 1u);
-    }
-  }
-  return g0;
-}
-__device__ __forceinline__ void lf_bar_wait(GridBar* b, unsigned g0, unsigned* err) {
-  if (threadIdx.x == 0) {
-    bool done = false;
-    for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
-      unsigned g;
-      asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(&b->gen) : "memory");
-      done = (g != g0);
-    }
-    if (!done) atomicOr(err, kErrTimeout);
-    asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
-  }
-  __syncthreads();
 }
 
 // K-slice GEMV step shared by phases A and C: this warp's GW groups of 16
@@ -186,25 +168,271 @@ __device__ __forceinline__ void lf_tile_dot(const uint8_t* slot, const uint32_t 
   }
 }
 
-// Issue one GEMV tile slice into this warp's ring slot: rows r_a (=gq) and
-// r_b (=gq+8) of the tile, groups [warp*GW, (warp+1)*GW), plus the 4-byte
-// scale pairs of the tile's 16 rows (lanes 0..15).
-template <int GW>
-__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, const uint8_t* qa, const uint8_t* qb,
-                                              const uint16_t* srow_lane, int warp, int lane) {
-  const int tq = lane & 3;
+// Issue one GEMV tile slice into this warp's ring slot: groups [warp*GW,
+// (warp+1)*GW) of the tile's 16 rows (row(r) gives the row index of tile row
+// r), plus the 4-byte scale words of the 16 rows (lanes 0..15).  Slot layout
+// (read by lf_tile_dot): [group gi][rows 0-7 | rows 8-15][lane (row&7)*4 + tq]
+// x 16 bytes.  With GW == 2 a warp's slice of a row is one aligned 128-byte
+// line, so each instruction fetches 4 whole lines (8 lanes per row); with
+// GW == 1 it is 64 bytes (4 lanes per row, 8 rows per instruction).
+template <int GW, class RowFn>
+__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, const uint8_t* base, const uint16_t* sbase,
+                                              int rowb, int scw, RowFn row, int warp, int lane) {
+  if (GW == 2) {
+    const int rsub = lane >> 3, c = lane & 7, gi = c >> 2, tq = c & 3;
 #pragma unroll
-  for (int gi = 0; gi < GW; ++gi) {
-    const int off = (warp * GW + gi) * kGroupBytes + tq * 16;
-    cp_async16_lf(slot + (gi * 2 + 0) * 512 + lane * 16, qa + off);
-    cp_async16_lf(slot + (gi * 2 + 1) * 512 + lane * 16, qb + off);
+    for (int j = 0; j < 4; ++j) {
+      const int r = 4 * j + rsub;
+      cp_async16_lf(slot + (gi * 2 + (r >> 3)) * 512 + ((r & 7) * 4 + tq) * 16,
+                    base + (size_t)row(r) * rowb + warp * 128 + c * 16);
+    }
+  } else {
+    const int gq = lane >> 2, tq = lane & 3;
+    const int off = warp * kGroupBytes + tq * 16;
+    cp_async16_lf(slot + lane * 16, base + (size_t)row(gq) * rowb + off);
+    cp_async16_lf(slot + 512 + lane * 16, base + (size_t)row(gq + 8) * rowb + off);
   }
   if (lane < 16) {
     // GW == 2: the 4 bytes [4 warp, 4 warp + 4); GW == 1: 2 bytes, copy the
     // aligned 4-byte word containing them.
-    const uint16_t* p = srow_lane + ((warp * GW) & ~1);
+    const uint16_t* p = sbase + (size_t)row(lane) * scw + ((warp * GW) & ~1);
     cp_async4_lf(slot + GW * 1024 + lane * 4, p);
   }
+}
+
+// Selection parameters of one call, written by the coordinating CTA (CTA 0)
+// once every worker has arrived, read by the workers.
+constexpr int kLfMaxCtas = 160;
+// Words written once per call carry the call's tag (bit 31 set, never 0) in
+// their upper half, so a reader polls the word itself and needs no separate
+// flag: 64-bit stores and loads are single-copy atomic.
+struct LfSel {
+  unsigned long long done;  // final barrier: arrivals of all calls so far (grows by gridDim.x per call)
+  unsigned pad_done[30];
+  unsigned coarse[256];  // coarse |g| histogram (one bin per bf16 exponent); zero between calls
+  unsigned maxkey;       // largest valid |g| key (atomicMax by the workers); zero between calls
+  unsigned pad0[31];
+  unsigned long long par[4];             // tagged: lo bits, hi bits, totA, filled
+  unsigned long long pre[kLfMaxCtas][2];  // tagged, per worker: tier A, tier B counts before it
+  unsigned long long cnt[kLfMaxCtas];     // per worker: 1<<63 | tier A << 32 | tier B; zero between calls
+  unsigned fine[kTopkHistBins];  // fine |g| histogram (one bin per key); zero between calls
+};
+__device__ __forceinline__ unsigned lf_tag(unsigned long long done0) {
+  return (unsigned)(done0 + 1u) | 0x80000000u;
+}
+__device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];\n" : "=l"(v) : "l"(p));
+  return v;
+}
+// Final grid barrier: one release-add per CTA on a counter that only grows,
+// each CTA polls the counter itself until the call's last arrival (the next
+// multiple of the grid size).  Bounded like grid_sync.
+__device__ __forceinline__ void lf_final_barrier(unsigned long long* done, unsigned* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long nb = gridDim.x;
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;\n" : "=l"(old) : "l"(done) : "memory");
+    const unsigned long long target = old - old % nb + nb;
+    bool ok = old + 1 == target;
+    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+      unsigned long long v;
+      asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(done) : "memory");
+      ok = v >= target;
+    }
+    if (!ok) atomicOr(err, kErrTimeout);
+    asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+  }
+  __syncthreads();
+}
+__device__ __forceinline__ unsigned long long lf_tagged(unsigned tag, unsigned v) {
+  return ((unsigned long long)tag << 32) | v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Gate rows of worker CTA b (1..nb-1); CTA 0 only coordinates.
+__device__ __forceinline__ int lf_row_start(int I, int nwk, int w) {
+  return I * w / nwk;  // I * w < 2^31 (checked on the host)
+}
+
+// CTA 0 coordinates one call in two releases (tagged words of LfSel):
+//   1. once every worker has arrived: the (K+1)-th largest key w from the
+//      coarse and fine histograms, topk_select.cu's 25-step fp32 bisection run
+//      on w, the tier totals -> lo, hi, totA, filled; release 1
+//   2. once every worker has published its tier A / tier B counts: their
+//      exclusive prefix -> pre[]; release 2
+// It clears the coarse histogram, the max word and the count words it read;
+// the workers clear the fine bins they filled.
+__device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* sel, int K, int nb,
+                                           unsigned tag) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwk = nb - 1;
+  __shared__ int s_cnt[2 * kLfMaxCtas];
+  if (tid == 0) {
+    bool ok = false;
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+      unsigned c;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(c) : "l"(&bar->count) : "memory");
+      if (c >= (unsigned)nwk) { ok = true; break; }
+    }
+    if (!ok) atomicOr(err, kErrTimeout);
+    __threadfence();
+  }
+  __syncthreads();
+  LF_CTA(13);
+  if (warp == 0) {
+    // coarse suffix sums, 8 bins per lane from the top
+    int c8[8], loc = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { c8[q] = (int)ld_cg_u32(sel->coarse + 255 - (lane * 8 + q)); loc += c8[q]; }
+    const unsigned maxkey = ld_cg_u32(&sel->maxkey);
+    int incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int suf8[8], run = incl - loc;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { run += c8[q]; suf8[q] = run; }
+    auto suffix_at = [&](int bin) -> int {  // #keys in coarse bins >= bin (warp-uniform bin)
+      if (bin >= 256) return 0;
+      const int src = (255 - bin) >> 3, q = (255 - bin) & 7;
+      int v = 0;
+#pragma unroll
+      for (int qq = 0; qq < 8; ++qq) v = (qq == q) ? suf8[qq] : v;
+      return __shfl_sync(0xffffffffu, v, src);
+    };
+    const int nvalid = __shfl_sync(0xffffffffu, run, 31);
+    const bool has_w = nvalid >= K + 1;
+    int b1 = -1;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (suf8[q] - c8[q] < K + 1 && K + 1 <= suf8[q]) b1 = 255 - (lane * 8 + q);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) b1 = max(b1, __shfl_xor_sync(0xffffffffu, b1, o));
+    // fine bins of b1 - 1, b1, b1 + 1 in one round: lo and hi end within a
+    // key of w, so the tier totals come from these bins too
+    int fb[3][4];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const int cb = b1 - 1 + d;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        fb[d][q] = (has_w && cb >= 0 && cb < 256) ? (int)ld_cg_u32(sel->fine + ((cb << 7) | (lane * 4 + q))) : 0;
+    }
+    float wv = 0.f;
+    if (has_w) {
+      const int rank = K + 1 - suffix_at(b1 + 1);
+      const int ls = fb[1][0] + fb[1][1] + fb[1][2] + fb[1][3];
+      int suf = ls;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += t;
+      }
+      int runf = suf - ls, found = -1;
+#pragma unroll
+      for (int q = 3; q >= 0; --q) {
+        runf += fb[1][q];
+        if (found < 0 && runf >= rank && runf - fb[1][q] < rank) found = lane * 4 + q;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(0xffffffffu, found, o));
+      wv = bf16_bits_to_f32((unsigned)((b1 << 7) | found));
+    }
+    // topk_select.cu's bisection: hi from the fp32 max of |g|, 25 halvings,
+    // "count(> t) > k" decided exactly by "w > t"
+    float hi = bf16_bits_to_f32(maxkey), lo = 0.0f;
+    float t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+#pragma unroll
+    for (int step = 0; step < 25; ++step) {
+      const bool up = has_w && wv > t;
+      lo = up ? t : lo;
+      hi = up ? hi : t;
+      t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    }
+    // #keys > tt = #keys >= kmin, kmin the bf16 key just above tt
+    auto count_above = [&](float tt) -> int {
+      const int kmin = (int)(__float_as_uint(tt) >> 16) + 1;
+      if (kmin > 0x7F80) return 0;
+      const int cb = kmin >> 7, f0 = kmin & 127, d = cb - (b1 - 1);
+      const bool held = has_w && d >= 0 && d < 3;
+      int part = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int f = lane * 4 + q;
+        if (f >= f0) part += held ? (d == 0 ? fb[0][q] : d == 1 ? fb[1][q] : fb[2][q])
+                                  : (int)ld_cg_u32(sel->fine + ((cb << 7) | f));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      return part + suffix_at(cb + 1);
+    };
+    const int totA = count_above(hi), above_lo = count_above(lo);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) sel->coarse[255 - (lane * 8 + q)] = 0u;
+    if (lane < 4) {  // release 1
+      const unsigned v = lane == 0 ? __float_as_uint(lo) : lane == 1 ? __float_as_uint(hi)
+                       : lane == 2 ? (unsigned)totA : (unsigned)min(K, above_lo);
+      sel->par[lane] = lf_tagged(tag, v);
+    }
+    if (lane == 0) {
+      sel->maxkey = 0u;
+      atomicExch(&bar->count, 0u);  // every worker has arrived
+    }
+  }
+  LF_CTA(14);
+  // round 2: every worker's (tier A, tier B) count word, prefix, release 2
+  for (int i = tid; i < 2 * kLfMaxCtas; i += kLfThreads) s_cnt[i] = 0;
+  __syncthreads();
+  if (tid >= 1 && tid <= nwk) {
+    unsigned long long v = 0;
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+      asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(sel->cnt + tid) : "memory");
+      if (v >> 63) break;
+    }
+    if (!(v >> 63)) { atomicOr(err, kErrTimeout); v = 0; }
+    sel->cnt[tid] = 0ull;
+    s_cnt[2 * (tid - 1)] = (int)((v >> 32) & 0x7FFFFFFF);
+    s_cnt[2 * (tid - 1) + 1] = (int)(v & 0xFFFFFFFFu);
+  }
+  __syncthreads();
+  LF_CTA(21);
+  if (warp == 0) {
+    int va[5], vb[5], la = 0, lb = 0;
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+      const int c = lane * 5 + q;
+      va[q] = c < nwk ? s_cnt[2 * c] : 0;
+      vb[q] = c < nwk ? s_cnt[2 * c + 1] : 0;
+      la += va[q];
+      lb += vb[q];
+    }
+    int ia = la, ib = lb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ta = __shfl_up_sync(0xffffffffu, ia, o), tb = __shfl_up_sync(0xffffffffu, ib, o);
+      if (lane >= o) { ia += ta; ib += tb; }
+    }
+    int pa = ia - la, pb = ib - lb;
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {  // release 2
+      const int c = lane * 5 + q;
+      if (c < nwk) {
+        sel->pre[c + 1][0] = lf_tagged(tag, (unsigned)pa);
+        sel->pre[c + 1][1] = lf_tagged(tag, (unsigned)pb);
+      }
+      pa += va[q];
+      pb += vb[q];
+    }
+  }
+  LF_CTA(22);
 }
 
 template <int GW>
@@ -215,35 +443,42 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   const int gq = lane >> 2, tq = lane & 3;
   const int H = a.hidden, I = a.inter, K = a.k;
   const int rowb = H / 2, scw = H / kGroup;  // bytes per packed row, scales per row
+  const int nb = gridDim.x, b = blockIdx.x, nwk = nb - 1;
+  LfSel* sel = reinterpret_cast<LfSel*>(a.scratch);
+  LF_CTA(0);
+
+  if (b == 0) {
+    pdl_wait();
+    lf_coordinate(a.bar, a.err, sel, K, nb, lf_tag(ld_cg_u64(&sel->done)));
+  } else {
   uint8_t* ring = smem + warp * kLfDepth * Geo::slot;
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Geo::xs);
   float* gsum = reinterpret_cast<float*>(smem + Geo::gsum);
   float* red = reinterpret_cast<float*>(smem + Geo::red);
-  int* rowp = reinterpret_cast<int*>(smem + Geo::rowp);
-  float* hv = reinterpret_cast<float*>(smem + Geo::hv);
+  uint16_t* gloc = reinterpret_cast<uint16_t*>(smem + Geo::gloc);
   float* misc = reinterpret_cast<float*>(smem + Geo::misc);
-  const int nb = gridDim.x, b = blockIdx.x;
   // GW == 1 reads the scale of group `warp` from the 4-byte word copied at
   // (warp & ~1); GW == 2 reads both halves.
   const int sc_sel = (GW == 1) ? (warp & 1) : 0;
+  // this call's tag (from the final barrier's counter, which grows once per call)
+  __shared__ unsigned s_tag;
 
   // ------------------------------------------------------------ phase A
-  const int ra0 = (int)((int64_t)I * b / nb), ra1 = (int)((int64_t)I * (b + 1) / nb);
+  const int ra0 = lf_row_start(I, nwk, b - 1), ra1 = lf_row_start(I, nwk, b);
   const int na = ra1 - ra0, nta = (na + 15) / 16;
   auto issue_a = [&](int i) {
     if (i < nta) {
-      const int ra = min(ra0 + i * 16 + gq, ra1 - 1), rb = min(ra0 + i * 16 + gq + 8, ra1 - 1);
-      const int rs = min(ra0 + i * 16 + (lane & 15), ra1 - 1);
-      lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.gate_qw + (size_t)ra * rowb,
-                        a.gate_qw + (size_t)rb * rowb, a.gate_sc + (size_t)rs * scw, warp, lane);
+      const int rbase = ra0 + i * 16, rlast = ra1 - 1;
+      lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.gate_qw, a.gate_sc, rowb, scw,
+                        [&](int r) { return min(rbase + r, rlast); }, warp, lane);
     }
     cp_commit_lf();
   };
 #pragma unroll
   for (int i = 0; i < kLfDepth - 1; ++i) issue_a(i);
   LF_TRACE(0);
-  LF_CTA(0);
   pdl_wait();
+  if (tid == 0) s_tag = lf_tag(ld_cg_u64(&sel->done));
   LF_TRACE(1);
 
   // Layer input: x, or RMSNorm(x + resid); staged in the B-fragment order.
@@ -285,7 +520,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
           }
           v4[q] = pr;
         }
-        if (a.x_used && b == 0)
+        if (a.x_used && b == 1)
           *reinterpret_cast<uint4*>(a.x_used + wi * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
         uint4 o;
         o.x = __byte_perm(v4[0], v4[2], 0x5410);
@@ -325,6 +560,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     issue_a(i + kLfDepth - 1);
     cp_wait_lf();
     __syncwarp();
+    if (i == 0) LF_CTA(19);
     float pa, pb;
     lf_tile_dot<GW>(ring + (i % kLfDepth) * Geo::slot, xf, bias, lane, sc_sel, pa, pb);
     if (tq == 0) {
@@ -337,7 +573,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   LF_TRACE(3);
   LF_CTA(1);
   __syncthreads();
-  uint16_t* gloc = reinterpret_cast<uint16_t*>(smem + Geo::gloc);
   for (int r = tid; r < na; r += kLfThreads) {
     const int i = r >> 4, row = r & 15;
     float v = 0.f;
@@ -347,297 +582,233 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     gloc[r] = o;
   }
   __syncthreads();
-  // Histogram counts aggregated over the CTA first (SiLU's minimum piles ~1/8
-  // of all values into two or three fine bins, and per-row global atomics on
-  // those serialise): a shared-memory copy of the bins, in the ring (idle
-  // now); the first row to reach a bin later adds the bin's total.
+  // |g| histograms, aggregated over the CTA first in shared memory (the ring,
+  // idle now): SiLU's minimum piles ~1/8 of all values into two or three fine
+  // bins and a handful of coarse bins (exponents) take nearly every value, so
+  // per-row global atomics would serialise.  The first row to reach a bin
+  // adds the bin's total.  Plus the largest key (one atomicMax per CTA).
   {
-    unsigned* sfine = reinterpret_cast<unsigned*>(smem);            // [kTopkHistBins]
-    unsigned* scoarse = sfine + kTopkHistBins;                       // [256]
+    unsigned* sfine = reinterpret_cast<unsigned*>(smem);   // [kTopkHistBins]
+    unsigned* scoarse = sfine + kTopkHistBins;              // [256]
+    __shared__ unsigned s_kmax;
     const unsigned kk = tid < na ? (gloc[tid] & 0x7FFFu) : 0xFFFFu;
     const bool valid = kk <= 0x7F80u;
     if (valid) sfine[kk] = 0u;
     for (int i = tid; i < 256; i += kLfThreads) scoarse[i] = 0u;
+    if (tid == 0) s_kmax = 0u;
     __syncthreads();
     bool lead_f = false, lead_c = false;
     if (valid) {
       lead_f = atomicAdd(&sfine[kk], 1u) == 0u;
       lead_c = atomicAdd(&scoarse[kk >> 7], 1u) == 0u;
+      atomicMax(&s_kmax, kk);
     }
     __syncthreads();
-    if (lead_f) atomicAdd(&a.scratch[kk], sfine[kk]);
-    if (lead_c) atomicAdd(&a.scratch[kTopkHistBins + (kk >> 7)], scoarse[kk >> 7]);
+    if (lead_f) atomicAdd(&sel->fine[kk], sfine[kk]);
+    if (lead_c) atomicAdd(&sel->coarse[kk >> 7], scoarse[kk >> 7]);
+    if (tid == 0 && s_kmax) atomicMax(&sel->maxkey, s_kmax);
+  }
+  // arrive (no wait: the coordinator releases the selection later)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(&a.bar->count, 1u);
   }
   LF_TRACE(4);
   LF_CTA(2);
-  const unsigned gen1 = lf_bar_arrive(a.bar);
-  lf_bar_wait(a.bar, gen1, a.err);
-  LF_TRACE(5);
-  LF_CTA(8);
 
-  // ------------------------------------------------------------ phase B
-  __shared__ int coarse_suffix[257];
+  // ------------------------------------------------------------ speculation
+  // This CTA's nts*16 rows with the largest |g| (about its expected share of
+  // k, so nearly all of them end up selected): their up projection starts now,
+  // while the coordinator computes the exact selection.  T = the (nts*16)-th
+  // largest key by a 15-step radix select over the block's keys.
+  int* crow = reinterpret_cast<int*>(smem + Geo::lists);  // C list: spec rows, then rest rows
+  int* drow = crow + kLfListMax;         // D list: selected channels
+  int* dsrc = drow + kLfListMax;         // D entry -> C list position
+  float* dh = reinterpret_cast<float*>(dsrc + kLfListMax);  // D entry: g, then h
+  int* cpos = reinterpret_cast<int*>(dh + kLfListMax);      // local row -> C position or -1
   __shared__ int2 warp_tot[33];
-  __shared__ int2 s_off;
-  __shared__ int s_tot[2];
-  __shared__ float s_lohi[2];
-  if (warp == 0) {
-    const unsigned* coarse = a.scratch + kTopkHistBins;
-    int cnt[8], loc = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      int v;
-      asm volatile("ld.global.cg.s32 %0, [%1];\n" : "=r"(v) : "l"(coarse + 255 - (lane * 8 + q)));
-      cnt[q] = v;
-      loc += v;
+  for (int r = tid; r < na; r += kLfThreads) cpos[r] = -1;
+  const unsigned my_key = tid < na ? (gloc[tid] & 0x7FFFu) : 0xFFFFu;
+  const bool my_valid = my_key <= 0x7F80u;
+  const int nvalid_loc = __syncthreads_count(my_valid);
+  const int nts = min(na * K / I / 16, nvalid_loc / 16);  // na * K < 2^31 (host check)
+  if (nts > 0) {
+    const int nspec = nts * 16;
+    unsigned T = 0;
+    for (int bit = 14; bit >= 0; --bit) {
+      const unsigned cand = T | (1u << bit);
+      if (__syncthreads_count(my_valid && my_key >= cand) >= nspec) T = cand;
     }
-    int incl = loc;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
+    // keys > T all fit; keys == T by index while places remain
+    int2 tot;
+    const int2 off = block_excl_scan2(my_valid && my_key > T, my_valid && my_key == T, warp_tot, tot);
+    int pos = -1;
+    if (my_valid && my_key > T) pos = off.x;
+    if (my_valid && my_key == T && tot.x + off.y < nspec) pos = tot.x + off.y;
+    if (pos >= 0) {
+      crow[pos] = ra0 + tid;
+      cpos[tid] = pos;
     }
-    int run = incl - loc;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) { run += cnt[q]; coarse_suffix[255 - (lane * 8 + q)] = run; }
-    if (lane == 0) coarse_suffix[256] = 0;
-    __syncwarp();
-    LF_CTA(13);
-    const int nvalid = coarse_suffix[0];
-    const bool has_w = nvalid >= K + 1;
-    // highest non-empty coarse bin, and the coarse bin b1 holding the
-    // (K+1)-th largest key
-    int topb = -1, b1 = -1;
-    for (int bb = lane; bb < 256; bb += 32) {
-      if (coarse_suffix[bb] - coarse_suffix[bb + 1] > 0) topb = max(topb, bb);
-      if (coarse_suffix[bb + 1] < K + 1 && K + 1 <= coarse_suffix[bb]) b1 = bb;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      topb = max(topb, __shfl_xor_sync(0xffffffffu, topb, o));
-      b1 = max(b1, __shfl_xor_sync(0xffffffffu, b1, o));
-    }
-    // One round of fine-bin reads: the top bin, and bins b1-1, b1, b1+1 (the
-    // final lo and hi lie within a key of the (K+1)-th key, so their counts
-    // come from these bins; other bins are read on demand below).
-    const int32_t* fine = reinterpret_cast<const int32_t*>(a.scratch);
-    int ft[4], fb[3][4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int f = lane * 4 + q;
-      ft[q] = topb >= 0 ? ld_cg_i32(fine + ((topb << 7) | f)) : 0;
-#pragma unroll
-      for (int d = 0; d < 3; ++d) {
-        const int cb = b1 - 1 + d;
-        fb[d][q] = (has_w && cb >= 0 && cb < 256) ? ld_cg_i32(fine + ((cb << 7) | f)) : 0;
-      }
-    }
-    LF_CTA(14);
-    int maxkey = 0;
-    if (topb >= 0) {
-      int mk = -1;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (ft[q] != 0) mk = (topb << 7) | (lane * 4 + q);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mk = max(mk, __shfl_xor_sync(0xffffffffu, mk, o));
-      maxkey = max(mk, 0);
-    }
-    float wv = 0.f;
-    if (has_w) {
-      // the rank-th largest key of bin b1: suffix sums over the fine bins
-      const int rank = K + 1 - coarse_suffix[b1 + 1];
-      const int ls = fb[1][0] + fb[1][1] + fb[1][2] + fb[1][3];
-      int suf = ls;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += t;
-      }
-      int runf = suf - ls, found = -1;
-#pragma unroll
-      for (int q = 3; q >= 0; --q) {
-        runf += fb[1][q];
-        if (found < 0 && runf >= rank && runf - fb[1][q] < rank) found = lane * 4 + q;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(0xffffffffu, found, o));
-      wv = bf16_bits_to_f32((unsigned)((b1 << 7) | found));
-    }
-    // the reference's 25-step fp32 bisection, run on the exact (K+1)-th key
-    float hi = bf16_bits_to_f32((unsigned)maxkey), lo = 0.0f;
-    float t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-    for (int step = 0; step < 25; ++step) {
-      if (has_w && wv > t) lo = t; else hi = t;
-      t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-    }
-    // #keys > tt = #keys >= kmin, kmin = bf16 key just above tt
-    auto count_above = [&](float tt) -> int {
-      const int kmin = (int)(__float_as_uint(tt) >> 16) + 1;
-      if (kmin > 0x7F80) return 0;
-      const int cb = kmin >> 7, f0 = kmin & 127, d = cb - (b1 - 1);
-      const bool held = has_w && d >= 0 && d < 3;
-      int part = 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int f = lane * 4 + q;
-        if (f >= f0) {
-          const int v = held ? (d == 0 ? fb[0][q] : d == 1 ? fb[1][q] : fb[2][q])
-                             : ld_cg_i32(fine + ((cb << 7) | f));
-          part += v;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      return part + (cb < 255 ? coarse_suffix[cb + 1] : 0);
-    };
-    const int c0n = count_above(hi), c1n = count_above(lo);
-    if (lane == 0) { s_lohi[0] = lo; s_lohi[1] = hi; s_tot[0] = c0n; s_tot[1] = c1n; }
   }
   __syncthreads();
-  LF_CTA(9);
-  // Selection (topk_select.cu): every key > hi ("tier A", all of them fit),
-  // then keys in (lo, hi] ("tier B") in index order while positions remain,
-  // then zero indices up to K.  Tier A of this CTA's rows is known locally;
-  // tier B needs the B counts of the rows before this CTA's, counted below
-  // straight from g (complete since the barrier).
-  const float lo = s_lohi[0], hi = s_lohi[1];
-  const int totA = s_tot[0], filled = min(K, s_tot[1]), selB = filled - totA;
-  const uint16_t key = tid < na ? (gloc[tid] & 0x7FFF) : 0x7FFF;  // NaN: never selected
-  const float kv = bf16_bits_to_f32(key);
-  const bool isA = kv > hi;
-  const bool isB = kv > lo && kv <= hi;
-  int2 tot;
-  const int2 off = block_excl_scan2(isA, isB, warp_tot, tot);
-  // local channel list: this CTA's tier A rows, then its selected tier B rows
-  if (isA) {
-    rowp[off.x] = ra0 + tid;
-    hv[off.x] = bf16_bits_to_f32(gloc[tid]);
-  }
-  __syncthreads();
-  auto issue_c = [&](int i) {
-    const int ra = rowp[i * 16 + gq], rb = rowp[i * 16 + gq + 8];
-    const int rs = rowp[i * 16 + (lane & 15)];
-    lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.up_qw + (size_t)ra * rowb,
-                      a.up_qw + (size_t)rb * rowb, a.up_sc + (size_t)rs * scw, warp, lane);
-  };
-  LF_CTA(15);
-  // full tiles of tier A rows do not depend on the other CTAs: start them now
-  const int n_early = min(kLfDepth - 1, tot.x / 16);
-  for (int i = 0; i < n_early; ++i) {
-    issue_c(i);
-    cp_commit_lf();
-  }
-  LF_CTA(6);
-  {
-    // tier A and tier B counts of rows [0, ra0), 8 keys per 16-byte load
-    int pa = 0, pb = 0;
-    const int nv = ra0 >> 3;
-    auto tally = [&](uint32_t w2) {
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const float v = bf16_bits_to_f32((h2 ? (w2 >> 16) : w2) & 0x7FFFu);
-        pa += v > hi;
-        pb += v > lo && v <= hi;
-      }
-    };
-    for (int i2 = tid; i2 < nv; i2 += kLfThreads) {
-      uint32_t w0, w1, w2, w3;
-      asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                   : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                   : "l"(a.g + (size_t)i2 * 8));
-      tally(w0); tally(w1); tally(w2); tally(w3);
-    }
-    for (int e = nv * 8 + tid; e < ra0; e += kLfThreads) {
-      const float v = bf16_bits_to_f32(ld_cg_u16(a.g + e) & 0x7FFFu);
-      pa += v > hi;
-      pb += v > lo && v <= hi;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      pa += __shfl_xor_sync(0xffffffffu, pa, o);
-      pb += __shfl_xor_sync(0xffffffffu, pb, o);
-    }
-    if (lane == 0) warp_tot[warp] = make_int2(pa, pb);
-    __syncthreads();
-    if (tid == 0) {
-      int sa = 0, sb = 0;
-      for (int w = 0; w < kLfWarps; ++w) { sa += warp_tot[w].x; sb += warp_tot[w].y; }
-      s_off = make_int2(sa, sb);
-    }
-    __syncthreads();
-  }
-  LF_CTA(7);
-  const int preA = s_off.x, preB = s_off.y;
-  const int nB = max(0, min(tot.y, selB - preB));  // this CTA's selected tier B rows
-  if (isB && off.y < nB) {
-    rowp[tot.x + off.y] = ra0 + tid;
-    hv[tot.x + off.y] = bf16_bits_to_f32(gloc[tid]);
-    a.idx[totA + preB + off.y] = ra0 + tid;
-  }
-  if (isA && preA + off.x < K) a.idx[preA + off.x] = ra0 + tid;
-  {
-    const int per = (K - filled + nb - 1) / nb;
-    const int z0 = filled + b * per, z1 = min(K, z0 + per);
-    for (int i2 = z0 + tid; i2 < z1; i2 += kLfThreads) a.idx[i2] = 0;
-  }
-  // The K - filled zero indices select channel 0 that many times: CTA 0
-  // (owner of row 0) adds one list entry for it, its h scaled by the count.
-  int nloc = tot.x + nB;
-  const int pad_row = (b == 0 && filled < K) ? nloc : -1;
-  if (pad_row >= 0) {
-    if (tid == 0) {
-      rowp[nloc] = 0;
-      hv[nloc] = bf16_bits_to_f32(gloc[0]);
-    }
-    ++nloc;
-  }
-  const int ntc = (nloc + 15) / 16;
-  __syncthreads();
-  // pad the last tile with a valid row and h = 0
-  for (int r = nloc + tid; r < ntc * 16; r += kLfThreads) {
-    rowp[r] = rowp[nloc - 1];
-    hv[r] = 0.f;
-  }
-  __syncthreads();
-  LF_TRACE(6);
   LF_CTA(3);
 
   // ------------------------------------------------------------ phases C + D
-  // One cp.async stream per warp: the ntc up tiles, then the ntc down tiles
-  // of the same channels (the first down tiles are in flight while h is formed).
+  // One cp.async stream per warp: spec up tiles, rest up tiles (this CTA's
+  // tier A rows and tie candidates outside the speculation), then the down
+  // tiles of the selected rows.
+  __shared__ float s_lohi[2];
+  __shared__ int s_par[4];
+  __shared__ int s_n[2];
+  int nC = nts, nD = 0, nDA = 0;
+  bool have1 = false, have2 = false;
+  auto issue_c = [&](int i) {
+    const int* rp = crow + i * 16;
+    lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.up_qw, a.up_sc, rowb, scw,
+                      [&](int r) { return rp[r]; }, warp, lane);
+  };
   const int seg = warp * GW * kGroupBytes;
-  auto issue_d = [&](int i) {
-    uint8_t* slot = ring + ((ntc + i) % kLfDepth) * Geo::slot;
-    // 16 rows x GW*64 bytes = 16*GW*4 chunks of 16 B
+  auto issue_d = [&](int j) {  // j: stream index; D tile j - nC
+    const int i = j - nC;
+    uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
 #pragma unroll
     for (int q = 0; q < (16 * GW * 4) / 32; ++q) {
       const int chk = lane + 32 * q;
       const int r = chk / (GW * 4), part = chk % (GW * 4);
-      const int ch = rowp[i * 16 + r];
+      const int ch = drow[i * 16 + r];
       cp_async16_lf(slot + r * kLfDnPitch + part * 16, a.dn_qw + (size_t)ch * rowb + seg + part * 16);
     }
     if (lane < 16) {
-      const int ch = rowp[i * 16 + lane];
+      const int ch = drow[i * 16 + lane];
       cp_async4_lf(slot + 16 * kLfDnPitch + lane * 4, a.dn_sc + (size_t)ch * scw + ((warp * GW) & ~1));
     }
   };
   auto issue = [&](int j) {
-    if (j < ntc) issue_c(j);
-    else if (j < 2 * ntc) issue_d(j - ntc);
+    if (j < nC) issue_c(j);
+    else if (j < nC + nD) issue_d(j);
     cp_commit_lf();
   };
-  for (int j = n_early; j < kLfDepth - 1; ++j) issue(j);
-  float acc[GW][8][4];
+  // Tier A ("> hi") and tier B ("in (lo, hi]") of topk_select.cu; NaN for rows past na.
+  const float kv = bf16_bits_to_f32(my_key);
+  bool isA = false, isB = false;
+  int2 offAB = make_int2(0, 0), totAB = make_int2(0, 0);
+  // Release 1: the thresholds.  Publish this CTA's tier counts, clear the fine
+  // bins it filled, queue the up rows of its tier A rows and tie candidates
+  // not speculated on, and list its tier A rows for the down projection.
+  auto need1 = [&]() {
+    if (tid == 0) {
+      const unsigned tag = s_tag;
+      unsigned long long p[4];
+      bool done = false;
+      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
 #pragma unroll
-  for (int u = 0; u < GW; ++u)
-#pragma unroll
-    for (int m = 0; m < 8; ++m) acc[u][m][0] = acc[u][m][1] = acc[u][m][2] = acc[u][m][3] = 0.f;
-  float colsum[GW];
-#pragma unroll
-  for (int u = 0; u < GW; ++u) colsum[u] = 0.f;
-  const int tpair = lane & 7, twhich = (lane >> 3) & 1;
-  for (int j = 0; j < ntc; ++j) {
+        for (int q = 0; q < 4; ++q) p[q] = ld_relaxed_u64(sel->par + q);
+        done = (unsigned)(p[0] >> 32) == tag && (unsigned)(p[1] >> 32) == tag &&
+               (unsigned)(p[2] >> 32) == tag && (unsigned)(p[3] >> 32) == tag;
+      }
+      if (!done) atomicOr(a.err, kErrTimeout);
+      s_lohi[0] = __uint_as_float((unsigned)p[0]);
+      s_lohi[1] = __uint_as_float((unsigned)p[1]);
+      s_par[0] = (int)(unsigned)p[2];
+      s_par[1] = (int)(unsigned)p[3];
+    }
+    __syncthreads();
+    LF_CTA(8);
+    const float lo = s_lohi[0], hi = s_lohi[1];
+    isA = kv > hi;
+    isB = kv > lo && kv <= hi;
+    offAB = block_excl_scan2(isA, isB, warp_tot, totAB);
+    if (tid == 0) {
+      const unsigned long long word =
+          (1ull << 63) | ((unsigned long long)totAB.x << 32) | (unsigned)totAB.y;
+      asm volatile("st.release.gpu.global.u64 [%0], %1;\n" ::"l"(sel->cnt + b), "l"(word) : "memory");
+    }
+    if (my_valid) sel->fine[my_key] = 0u;
+    // the owner of row 0 may need channel 0 for the index padding
+    const bool pad_maybe = b == 1 && s_par[1] < K;
+    const bool restr = tid < na && (isA || isB || (pad_maybe && tid == 0)) && cpos[tid] < 0;
+    int2 t2;
+    const int2 o2 = block_excl_scan2(restr, false, warp_tot, t2);
+    if (restr) {
+      crow[nts * 16 + o2.x] = ra0 + tid;
+      cpos[tid] = nts * 16 + o2.x;
+    }
+    __syncthreads();
+    const int nrest = t2.x, ntr = (nrest + 15) / 16;
+    for (int r = nrest + tid; r < ntr * 16; r += kLfThreads) crow[nts * 16 + r] = crow[nts * 16 + nrest - 1];
+    if (isA) {  // down list: tier A rows first
+      drow[offAB.x] = ra0 + tid;
+      dsrc[offAB.x] = cpos[tid];
+      dh[offAB.x] = bf16_bits_to_f32(gloc[tid]);
+    }
+    nC = nts + ntr;
+    nDA = totAB.x;
+    __syncthreads();
+  };
+  // Release 2: this CTA's prefix counts.  Write its part of idx, append the
+  // selected tie rows and the padding entry to the down list.
+  auto need2 = [&]() {
+    if (tid == 0) {
+      const unsigned tag = s_tag;
+      unsigned long long p0 = 0, p1 = 0;
+      bool done = false;
+      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+        p0 = ld_relaxed_u64(&sel->pre[b][0]);
+        p1 = ld_relaxed_u64(&sel->pre[b][1]);
+        done = (unsigned)(p0 >> 32) == tag && (unsigned)(p1 >> 32) == tag;
+      }
+      if (!done) atomicOr(a.err, kErrTimeout);
+      s_par[2] = (int)(unsigned)p0;
+      s_par[3] = (int)(unsigned)p1;
+    }
+    __syncthreads();
+    LF_CTA(9);
+    const int totA = s_par[0], filled = s_par[1], selB = filled - totA;
+    const int preA = s_par[2], preB = s_par[3];
+    const int nB = max(0, min(totAB.y, selB - preB));
+    if (isA && preA + offAB.x < K) a.idx[preA + offAB.x] = ra0 + tid;
+    if (isB && offAB.y < nB) {
+      a.idx[totA + preB + offAB.y] = ra0 + tid;
+      drow[nDA + offAB.y] = ra0 + tid;
+      dsrc[nDA + offAB.y] = cpos[tid];
+      dh[nDA + offAB.y] = bf16_bits_to_f32(gloc[tid]);
+    }
+    {
+      const int per = (K - filled + nwk - 1) / nwk;
+      const int z0 = filled + (b - 1) * per, z1 = min(K, z0 + per);
+      for (int i2 = z0 + tid; i2 < z1; i2 += kLfThreads) a.idx[i2] = 0;
+    }
+    // The K - filled zero indices select channel 0 that many times: the
+    // owner of row 0 adds one down entry for it, h scaled by the count.
+    const bool pad = b == 1 && filled < K;
+    const int nd = nDA + nB + (pad ? 1 : 0);
+    if (tid == 0) {
+      if (pad) {
+        drow[nDA + nB] = 0;
+        dsrc[nDA + nB] = cpos[0];
+        dh[nDA + nB] = bf16_bits_to_f32(gloc[0]);
+      }
+      s_n[0] = pad ? nDA + nB : -1;
+      s_n[1] = K - filled;
+    }
+    __syncthreads();
+    const int ntd = (nd + 15) / 16;
+    for (int r = nd + tid; r < ntd * 16; r += kLfThreads) {
+      drow[r] = drow[nd - 1];
+      dsrc[r] = -1;
+    }
+    nD = ntd;
+    __syncthreads();
+  };
+  auto need = [&](int j) {  // before issuing stream index j
+    if (!have1 && j >= nts) { need1(); have1 = true; }
+    if (have1 && !have2 && j >= nC) { need2(); have2 = true; }
+  };
+#pragma unroll 1
+  for (int j = 0; j < kLfDepth - 1; ++j) { need(j); issue(j); }
+  for (int j = 0; j < nC; ++j) {
+    need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
     cp_wait_lf();
     __syncwarp();
@@ -649,26 +820,44 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
     __syncwarp();
   }
-  // h = bf16(g * bf16(u)) for the whole list (padding rows give 0) while the
-  // first down tiles are in flight
+  // h = bf16(g * bf16(u)) for the down list, while its first tiles are in flight
   __syncthreads();
-  for (int r = tid; r < ntc * 16; r += kLfThreads) {
-    const int ti = r >> 4, row = r & 15;
-    float v = 0.f;
-    for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
-    float h = r < nloc ? round_bf16(hv[r] * round_bf16(v)) : 0.f;
-    if (r == pad_row) h *= (float)(K - filled);
-    hv[r] = h;
+  {
+    const int pad_row = s_n[0];
+    const float mult = (float)s_n[1];
+    for (int r = tid; r < nD * 16; r += kLfThreads) {
+      const int src = dsrc[r];
+      float h = 0.f;
+      if (src >= 0) {
+        const int ti = src >> 4, row = src & 15;
+        float v = 0.f;
+        for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
+        h = round_bf16(dh[r] * round_bf16(v));
+        if (r == pad_row) h *= mult;
+      }
+      dh[r] = h;
+    }
   }
   __syncthreads();
   LF_TRACE(7);
   LF_CTA(10);
-  for (int j = ntc; j < 2 * ntc; ++j) {
+  float acc[GW][8][4];
+#pragma unroll
+  for (int u = 0; u < GW; ++u)
+#pragma unroll
+    for (int m = 0; m < 8; ++m) acc[u][m][0] = acc[u][m][1] = acc[u][m][2] = acc[u][m][3] = 0.f;
+  float colsum[GW];
+#pragma unroll
+  for (int u = 0; u < GW; ++u) colsum[u] = 0.f;
+  const int tpair = lane & 7, twhich = (lane >> 3) & 1;
+  for (int j = nC; j < nC + nD; ++j) {
+    need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
     cp_wait_lf();
     __syncwarp();
+    if (j == nC) LF_CTA(17);
     const uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
-    const int i = j - ntc;
+    const int i = j - nC;
 #pragma unroll
     for (int u = 0; u < GW; ++u) {
       uint32_t bval = 0;
@@ -679,7 +868,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
           const int c = 2 * tpair + e;
           const uint16_t* sp = reinterpret_cast<const uint16_t*>(slot + 16 * kLfDnPitch + c * 4);
           const int sidx = (GW == 1) ? (warp & 1) : u;
-          const float hs = hv[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
+          const float hs = dh[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
           const float h1 = round_bf16(hs);
           v2[e] = twhich ? round_bf16(hs - h1) : h1;
         }
@@ -714,7 +903,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   LF_TRACE(9);
   LF_CTA(4);
-  pdl_launch_dependents();
 #pragma unroll
   for (int u = 0; u < GW; ++u) {
     float cs = colsum[u];
@@ -736,66 +924,67 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   }
   LF_TRACE(10);
   LF_CTA(5);
-  grid_sync(a.bar, a.err);
+  }  // worker
+  pdl_launch_dependents();
+  lf_final_barrier(&sel->done, a.err);
   LF_TRACE(11);
   LF_CTA(11);
 
   // ------------------------------------------------------------ phase E
-  // The histograms have no readers left: clear it
-  // for the next call, spread over the CTAs.
+  // y[4q .. 4q+3] for this CTA's quads (at most 10): two warps per quad, lane
+  // l of the pair sums workers 1 + l, 1 + l + 64, ...; then a fixed shuffle
+  // tree and the pair's sum.
   {
-    const int nwords = kTopkHistBins + 256;
-    const int per = (nwords + nb - 1) / nb;
-    for (int i2 = b * per + tid; i2 < min(nwords, (b + 1) * per); i2 += kLfThreads) a.scratch[i2] = 0u;
-  }
-  // y[4q .. 4q+3] for this CTA's quads: R row-lanes per quad each sum every
-  // R-th partial vector, then a fixed-shape tree over the R lanes.
-  {
+    float* red = reinterpret_cast<float*>(smem + Geo::red);
     const int n4 = H >> 2;
-    const int q0 = (int)((int64_t)n4 * b / nb), q1 = (int)((int64_t)n4 * (b + 1) / nb);
-    const int nq = q1 - q0;
-    if (nq > 0) {
-      int R = 64;
-      while (R > 1 && R * nq > kLfThreads) R >>= 1;
-      float4* e4 = reinterpret_cast<float4*>(red);
-      const int q = tid % nq, rr = tid / nq;
-      if (rr < R) {
-        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = rr; c < nb; c += R) {
-          float4 v;
+    const int q0 = n4 * b / nb, q1 = n4 * (b + 1) / nb;
+    const int nq = q1 - q0;  // <= 10 (checked on the host)
+    const int q = warp >> 1, l64 = (warp & 1) * 32 + lane;
+    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q < nq) {
+      float4 v[3];  // nb <= 160: at most 3 partial rows per lane, loaded together
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        const int c = 1 + l64 + 64 * u;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < nb)
           asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];\n"
-                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                       : "=f"(v[u].x), "=f"(v[u].y), "=f"(v[u].z), "=f"(v[u].w)
                        : "l"(a.partial + (size_t)c * H + 4 * (q0 + q)));
-          s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
-        }
-        e4[rr * nq + q] = s4;
       }
-      __syncthreads();
-      for (int st = R >> 1; st > 0; st >>= 1) {
-        if (rr < st) {
-          const float4 o = e4[(rr + st) * nq + q];
-          float4& m = e4[rr * nq + q];
-          m.x += o.x; m.y += o.y; m.z += o.z; m.w += o.w;
-        }
-        __syncthreads();
+#pragma unroll
+      for (int u = 0; u < 3; ++u) { s4.x += v[u].x; s4.y += v[u].y; s4.z += v[u].z; s4.w += v[u].w; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s4.x += __shfl_xor_sync(0xffffffffu, s4.x, o);
+      s4.y += __shfl_xor_sync(0xffffffffu, s4.y, o);
+      s4.z += __shfl_xor_sync(0xffffffffu, s4.z, o);
+      s4.w += __shfl_xor_sync(0xffffffffu, s4.w, o);
+    }
+    float4* e4 = reinterpret_cast<float4*>(red);
+    if (lane == 0 && (warp & 1)) e4[q] = s4;
+    __syncthreads();
+    LF_CTA(18);
+    if (lane == 0 && !(warp & 1) && q < nq) {
+      const float4 o4 = e4[q];
+      s4.x += o4.x; s4.y += o4.y; s4.z += o4.z; s4.w += o4.w;
+      const int o = 4 * (q0 + q);
+      if (a.y) {
+        a.y[o] = f32_to_bf16_bits(s4.x); a.y[o + 1] = f32_to_bf16_bits(s4.y);
+        a.y[o + 2] = f32_to_bf16_bits(s4.z); a.y[o + 3] = f32_to_bf16_bits(s4.w);
       }
-      if (rr == 0) {
-        const float4 s4 = e4[q];
-        const int o = 4 * (q0 + q);
-        if (a.y) {
-          a.y[o] = f32_to_bf16_bits(s4.x); a.y[o + 1] = f32_to_bf16_bits(s4.y);
-          a.y[o + 2] = f32_to_bf16_bits(s4.z); a.y[o + 3] = f32_to_bf16_bits(s4.w);
-        }
-        if (a.y_f32) *reinterpret_cast<float4*>(a.y_f32 + o) = s4;
-      }
+      if (a.y_f32) *reinterpret_cast<float4*>(a.y_f32 + o) = s4;
     }
   }
   LF_TRACE(12);
   LF_CTA(12);
 }
 
+constexpr size_t kLfSelBytes = (sizeof(LfSel) + 255) & ~size_t(255);
+
 size_t layer_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
-  const size_t s = ((topk_scratch_bytes() + 255) & ~size_t(255)) + 256 +
+  const size_t s = kLfSelBytes + 256 +
                    (((size_t)inter * 2 + 255) & ~size_t(255)) + (((size_t)k * 4 + 255) & ~size_t(255)) +
                    (size_t)num_sms() * hidden * 4;
   return s;
@@ -808,7 +997,7 @@ using namespace dip;
 extern "C" size_t dip_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k <= 0) return 0;
   // device independent upper bound (up to 160 SMs)
-  return ((topk_scratch_bytes() + 255) & ~size_t(255)) + 256 +
+  return kLfSelBytes + 256 +
          (((size_t)inter * 2 + 255) & ~size_t(255)) + (((size_t)k * 4 + 255) & ~size_t(255)) +
          (size_t)160 * hidden * 4;
 }
@@ -827,9 +1016,11 @@ extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, con
   if (H % kGroup == 0 && G == kLfWarps * 1) gw = 1;
   if (H % kGroup == 0 && G == kLfWarps * 2) gw = 2;
   if (!gw) return DIP_ERR_UNSUPPORTED;
-  // per-CTA limits: gate rows (= candidate channels) plus one padding entry
-  // <= 16*kLfTilesA, and at most one row per thread
-  if ((I + nb - 1) / nb > 16 * kLfTilesA - 1 || (I + nb - 1) / nb > kLfThreads)
+  // per-worker limits (CTA 0 coordinates): gate rows <= 16*kLfTilesA - 1
+  // (C list: rows plus one padding entry, in at most kLfTilesA + 1 tiles)
+  if (nb < 2 || (I + nb - 2) / (nb - 1) > 16 * kLfTilesA - 1 || I * (int64_t)nb >= (int64_t(1) << 31) ||
+      (H / 4 + nb - 1) / nb > kLfWarps / 2 ||
+      (int64_t)16 * kLfTilesA * k >= (int64_t(1) << 31))
     return DIP_ERR_UNSUPPORTED;
   if (workspace_bytes < dip_mlp_fused_workspace_bytes(H, I, k)) return DIP_ERR_WORKSPACE;
   const uintptr_t al = reinterpret_cast<uintptr_t>(L->gate_qw) | reinterpret_cast<uintptr_t>(L->up_qw) |
@@ -839,7 +1030,7 @@ extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, con
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   LfArgs a = {};
   a.scratch = reinterpret_cast<unsigned*>(ws);
-  ws += (topk_scratch_bytes() + 255) & ~size_t(255);
+  ws += kLfSelBytes;
   a.bar = reinterpret_cast<GridBar*>(ws);
   ws += 256;
   a.g = g_out ? g_out : reinterpret_cast<uint16_t*>(ws);
