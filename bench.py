@@ -29,6 +29,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "dynamic-input-pruning_b200"))
 sys.path.insert(0, str(REPO))
 
+RMS_EPS_BENCH = 1e-6
 METRIC = "dip_mlp_decode_tok_s"
 UNIT = "tok/s"
 
@@ -153,6 +154,27 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_single_layer(n):
+    """n launches of the fused kernel on one config-1 layer (a small, fixed case
+    for ncu captures: ~0.2 GB on the device, one kernel per launch)."""
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, make_layer
+    dev = torch.device("cuda", 0)
+    cfg = StackConfig(n_layers=1, seed=0)
+    L = make_layer(cfg, 0, dev)
+    ws = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(cfg.hidden, cfg.inter, cfg.k),
+                     dtype=torch.uint8, device=dev)
+    x = torch.randn(cfg.hidden, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    x = x.to(dev)
+    for _ in range(n):
+        y, _, _ = torch.ops.dip_b200.mlp_decode_fused(L["gate_qw"], L["gate_sc"], L["up_qw"],
+                                                      L["up_sc"], L["down_t_qw"], L["down_t_sc"],
+                                                      x, None, RMS_EPS_BENCH, cfg.k, ws)
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    print(json.dumps({"single_layer_launches": n, "y_abs_sum": float(y.float().abs().sum())}))
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     import dip_b200  # noqa: F401  (loads the kernels; raises if unbuilt)
@@ -217,23 +239,44 @@ def run_ours(args):
            "h2d_bytes_per_step": (x0[0].numel() + resid[0].numel()) * 2,
            "d2h_bytes_per_step": cfg.hidden * 2}
 
-    # dominant kernel: the gate GEMV + SiLU, timed per launch with events
+    # dominant kernel, timed per launch with CUDA events on the launching stream
     nb = layer_weight_bytes(cfg)
-    gate_ms = []
     xg = x0[0].contiguous()
+    evs = []
+    if stack.fused:
+        # the whole layer is one launch (layer_fused_kernel): every byte the
+        # layer must read is this kernel's algorithmic traffic
+        kern = "layer_fused_kernel (one decode layer: gate, exact top-k, gathered up/down)"
+        alg_bytes = nb["total"]
+        ws = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(cfg.hidden, cfg.inter,
+                                                                      cfg.k),
+                         dtype=torch.uint8, device=dev)
+
+        def one(L):
+            torch.ops.dip_b200.mlp_decode_fused(L["gate_qw"], L["gate_sc"], L["up_qw"],
+                                                L["up_sc"], L["down_t_qw"], L["down_t_sc"],
+                                                xg, None, 1e-6, cfg.k, ws)
+        traffic_key = "layer_fused_kernel"
+    else:
+        kern = "gate_silu (int4 GEMV + SiLU, 25600x5120)"
+        alg_bytes = nb["gate"]
+
+        def one(L):
+            torch.ops.dip_b200.gate_silu(L["gate_qw"], L["gate_sc"], xg)
+        traffic_key = "gate_silu"
     for rep in range(3):
-        for L in stack.layers:
+        for L in stack.layers:  # 64 distinct layers: each launch reads cold weights
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            torch.ops.dip_b200.gate_silu(L["gate_qw"], L["gate_sc"], xg)
+            one(L)
             b.record()
-            gate_ms.append((a, b))
+            evs.append((a, b))
     torch.cuda.synchronize()
-    durs = [a.elapsed_time(b) for a, b in gate_ms[len(stack.layers):]]
-    gate_avg = sum(durs) / len(durs)
+    durs = [a.elapsed_time(b) for a, b in evs[len(stack.layers):]]
+    kern_avg_ms = sum(durs) / len(durs)
     peak, peak_kind = _peaks()
-    achieved = nb["gate"] / (gate_avg / 1e3) / 1e9
-    traffic = _traffic().get("gate_silu")
+    achieved = alg_bytes / (kern_avg_ms / 1e3) / 1e9
+    traffic = _traffic().get(traffic_key)
     layer_us = ms_per_step * 1e3 / cfg.n_layers
     layer_gbs = nb["total"] / (layer_us / 1e6) / 1e9
 
@@ -250,11 +293,11 @@ def run_ours(args):
         "layer_hbm_gbs": layer_gbs,
         "layer_hbm_frac_of_measured": layer_gbs / peak,
         "layer_hbm_frac_of_8tbs": layer_gbs / 8000.0,
-        "roofline": {"kernel": "gate_silu (int4 GEMV + SiLU, 25600x5120)", "bound": "hbm",
+        "roofline": {"kernel": kern, "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes": nb["gate"],
-                     "avg_launch_us": gate_avg * 1e3},
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (burst copy)",
+                     "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                     "avg_launch_us": kern_avg_ms * 1e3},
         "e2e": e2e,
         "gpu_launches": args.steps * (cfg.n_layers if stack.fused else cfg.n_layers * 6 - 1),
         "path": args.path,
@@ -284,11 +327,15 @@ def main():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--cpu-layers", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--single-layer", type=int, default=0, metavar="N",
+                    help="profiling aid: N launches of one config-1 fused layer, then exit")
     ap.add_argument("--path", default="fused", choices=["fused", "chain"],
                     help="fused: one persistent kernel per layer; chain: separate launches")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
+    if args.single_layer:
+        run_single_layer(args.single_layer)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

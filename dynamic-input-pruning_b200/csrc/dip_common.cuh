@@ -161,8 +161,6 @@ unsigned* error_word_ptr();
 int gemv_silu_hist(const int8_t* qweight, const uint16_t* scales, const uint16_t* x,
                    uint16_t* out, int64_t rows, int64_t in_features, unsigned* hist,
                    cudaStream_t stream);
-int topk_from_hist_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx,
-                          unsigned* hist, cudaStream_t st);
 // Top-k scratch: fine histogram [32768], coarse histogram [256], look-back words.
 constexpr int kTopkHistBins = 32768;
 size_t topk_scratch_bytes();

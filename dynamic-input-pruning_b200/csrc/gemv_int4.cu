@@ -252,20 +252,7 @@ __device__ __forceinline__ void group_mma(const uint4& wa, const uint4& wb, cons
   }
 }
 
-// ---------------------------------------------------------------------------
-// Default variant: the same tile / fragment layout as gemv_int4_kernel, but
-// every weight byte a warp needs is requested up front with per-thread
-// asynchronous copies (cp.async, 16 B each) into a warp-private shared-memory
-// area, one commit group per quantisation group.  The warp then consumes the
-// groups in order with cp.async.wait_group, so all of a CTA's loads are in
-// flight at once without holding registers, and several CTAs per SM keep
-// ~150 KB per SM in flight.  A lane reads back only what it copied itself,
-// so no block barrier is needed between the copies and the math.  (A
-// producer-warp ring of 1-D bulk copies was measured slower on B200 for
-// rows of 1.3-2.6 KB: it saturated at 1.7-4.2 TB/s against 6.25 TB/s for
-// per-thread loads.)
-constexpr int kCpaMaxGroupsPerWarp = 16;  // in_features <= 8192
-
+// cp.async helpers of the streaming GEMV below.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem)
                : "memory");

@@ -268,111 +268,16 @@ ca_split_kernel(const int32_t* __restrict__ idx, int k, const int64_t* __restric
 // ---------------------------------------------------------------------------
 // Histogram-based top-k (the fast path).  The exact bisection emulation needs
 // only w, the (k+1)-th largest |s|, and max|s|; both come from a 32768-bin
-// histogram of the 15-bit magnitudes.  In the fused decode chain the gate
-// kernel fills the histogram in its epilogue (one global atomic per channel),
-// so the select kernel below only scans 128 KB and compacts.  It leaves the
-// histogram zero for the next call.
+// histogram of the 15-bit magnitudes.  In the decode chain the gate kernel
+// fills the histogram in its epilogue, so the select step only reads a few
+// slices of it and compacts; it leaves the histogram zero for the next call.
 constexpr int kHistBins = 32768;
-
-__global__ void __launch_bounds__(256)
-topk_hist_kernel(const uint16_t* __restrict__ s, int n, unsigned* __restrict__ hist) {
-  pdl_wait();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const unsigned key = s[i] & 0x7FFFu;
-    if (key <= 0x7F80u) atomicAdd(&hist[key], 1u);
-  }
-  pdl_launch_dependents();
-}
-
-__global__ void __launch_bounds__(kTopkThreads)
-topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __restrict__ idx,
-                      unsigned* __restrict__ hist) {
-  extern __shared__ __align__(16) uint16_t keys[];
-  __shared__ int2 warp_tot[33];
-  __shared__ unsigned s_max;
-  __shared__ unsigned s_w;
-  __shared__ float s_lohi[2];
-  const int tid = threadIdx.x;
-  if (tid == 0) { s_max = 0; s_w = 0; }
-  pdl_wait();
-  DIP_TRACE_POINT(0);
-  // Thread tid owns bins [32 tid, 32 tid + 32): counts, then zero them.
-  uint4* hv = reinterpret_cast<uint4*>(hist) + tid * 8;
-  unsigned c[32];
-  int tot_mine = 0;
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const uint4 v = hv[q];
-    c[4 * q] = v.x; c[4 * q + 1] = v.y; c[4 * q + 2] = v.z; c[4 * q + 3] = v.w;
-    tot_mine += v.x + v.y + v.z + v.w;
-  }
-#pragma unroll
-  for (int q = 0; q < 8; ++q) hv[q] = make_uint4(0, 0, 0, 0);
-  // Stage |s| for the compaction meanwhile.
-  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
-  const int nvec = vec ? n / 8 : 0;
-  for (int v = tid; v < nvec; v += kTopkThreads) {
-    uint4 r = __ldg(reinterpret_cast<const uint4*>(s) + v);
-    r.x &= 0x7FFF7FFFu; r.y &= 0x7FFF7FFFu; r.z &= 0x7FFF7FFFu; r.w &= 0x7FFF7FFFu;
-    reinterpret_cast<uint4*>(keys)[v] = r;
-  }
-  for (int i = nvec * 8 + tid; i < n; i += kTopkThreads) keys[i] = s[i] & 0x7FFF;
-  DIP_TRACE_POINT(1);
-  int2 tot;
-  const int2 pre = block_excl_scan2(tot_mine, 0, warp_tot, tot);  // also a barrier
-  DIP_TRACE_POINT(2);
-  const int nvalid = tot.x;
-  const int above = nvalid - pre.x - tot_mine;  // count in bins above my range
-  // Fully unrolled scans keep c[] in registers.
-  int top = -1;
-#pragma unroll
-  for (int b = 0; b < 32; ++b) if (c[b] != 0) top = b;
-  unsigned mkey = top >= 0 ? (unsigned)(tid * 32 + top) : 0u;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mkey = max(mkey, __shfl_xor_sync(0xffffffffu, mkey, o));
-  if ((tid & 31) == 0 && mkey) atomicMax(&s_max, mkey);
-  const bool has_w = nvalid >= k + 1;
-  if (has_w && above < k + 1 && k + 1 <= above + tot_mine) {
-    int run = above, found = -1;
-#pragma unroll
-    for (int b = 31; b >= 0; --b) {
-      run += c[b];
-      if (found < 0 && run >= k + 1) found = b;
-    }
-    s_w = (unsigned)(tid * 32 + found);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const float wv = bf16_bits_to_f32(s_w);
-    float hi = bf16_bits_to_f32(s_max);
-    float lo = 0.0f;
-    float t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-    for (int step = 0; step < 25; ++step) {
-      if (has_w && wv > t) lo = t; else hi = t;
-      t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
-    }
-    s_lohi[0] = lo;
-    s_lohi[1] = hi;
-  }
-  __syncthreads();
-  const float lo = s_lohi[0], hi = s_lohi[1];
-  DIP_TRACE_POINT(3);
-  block_compact2(
-      n, [&](int i) { return bf16_bits_to_f32(keys[i]) > hi; },
-      [&](int i) { const float v = bf16_bits_to_f32(keys[i]); return v > lo && v <= hi; },
-      [&](int pos, int i) { if (pos < k) idx[pos] = i; }, warp_tot, tot);
-  DIP_TRACE_POINT(4);
-  pdl_launch_dependents();
-  const int filled = min(k, tot.x + tot.y);
-  for (int i = filled + tid; i < k; i += kTopkThreads) idx[i] = 0;
-  DIP_TRACE_POINT(5);
-}
 
 // ---------------------------------------------------------------------------
 // Top-k v3: select from a two-level histogram, compact on many SMs.
 //
 // Scratch (dip_topk_hist_bytes): fine[32768] counts of the 15-bit |s| key,
-// coarse[256] counts of its exponent byte, status[64] look-back words.  It
+// coarse[256] counts of its exponent byte, status[256] look-back words.  It
 // must be zero on entry.  The selection reads only the coarse histogram and
 // three 128-bin slices of the fine one, so no SM moves more than a few
 // hundred bytes of it.  Each CTA then compacts its own 2048-element chunk:
@@ -382,7 +287,7 @@ topk_from_hist_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __r
 constexpr int kCoarseOff = kHistBins;                 // in u32 words
 constexpr int kStatusOffBytes = (kHistBins + 256) * 4;
 constexpr int kCompactChunk = 2048;                   // elements per CTA
-constexpr int kMaxCompactCtas = 256;  // also the look-back words of the fused layer kernel
+constexpr int kMaxCompactCtas = 256;
 constexpr size_t kTopkScratchBytes = kStatusOffBytes + kMaxCompactCtas * 8;
 
 // #{keys > t} from the histograms (t >= 0, fp32): keys above bf16 bin b0 =
@@ -581,18 +486,6 @@ int topk_compact_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, u
 }
 
 size_t topk_scratch_bytes() { return kTopkScratchBytes; }
-
-int topk_from_hist_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx,
-                          unsigned* hist, cudaStream_t st) {
-  if (n < 1 || n > kTopkMaxN || k < 1 || k > INT32_MAX || !s || !idx || !hist) return DIP_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(hist) & 15) != 0) return DIP_ERR_ARG;
-  const size_t smem = (size_t)n * 2;
-  cudaError_t e = cudaFuncSetAttribute(topk_from_hist_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return launch_status(e);
-  return launch_status(launch(topk_from_hist_kernel, dim3(1), dim3(kTopkThreads), smem, st, s,
-                              (int)n, (int)k, idx, hist));
-}
 
 int topk_launch(const uint16_t* s, int64_t n, int64_t k, int32_t* idx, int batch,
                 int64_t s_stride, int64_t idx_stride, cudaStream_t st) {

@@ -56,9 +56,10 @@ DIP_API int dip_set_pdl(int enable);
  * completed) and returned early; its outputs are then invalid.  Synchronous
  * (a device-to-host copy).  0 = no error recorded. */
 DIP_API int dip_take_device_error(unsigned int* out);
-/* Selects the kernel implementations: 0 (default) = the persistent bulk-copy
- * ring kernels (GEMV family and tensor-core down projection) where the shape
- * allows them, 1 = the simple kernels (one tile per CTA GEMV, CUDA-core down).
+/* Selects the kernel implementations: 0 (default) = the streaming kernels
+ * (K-slice cp.async GEMV family and tensor-core down projection) where the
+ * shape allows them, 1 = the simple kernels (one tile per CTA GEMV, CUDA-core
+ * down).
  * Both give the same values up to fp32 summation order; the switch exists
  * for testing and comparison.  Returns the previous setting. */
 DIP_API int dip_set_gemv_variant(int simple);
