@@ -175,6 +175,219 @@ def run_single_layer(n):
     print(json.dumps({"single_layer_launches": n, "y_abs_sum": float(y.float().abs().sum())}))
 
 
+def _time_stack(stack, x0, resid, warmup, steps, dev):
+    """Graph-replayed decode steps: warm-up, then `steps` timed with CUDA events."""
+    stack.capture()
+    xi, ri = stack._static_in
+    for t in range(warmup):
+        xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record()
+        for t in range(warmup, warmup + steps):
+            xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, clk.summary()
+
+
+def run_config2(args):
+    """Config 2: cache-aware DIP on the 64-layer stack with LogNormal(0,1)
+    gate-row scales; calibration on 32 N(0,1) tokens run through the DIP
+    stack, cache_n = 0.3 I hot channels per layer.  Reports us/layer and
+    tok/s of the CA path (and of the streaming fused path on the same
+    weights), the hit rate, and whether every recorded hit/miss split equals
+    its definition (hits then misses, each in top-k order) recomputed with
+    torch ops from the same indices."""
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, DipStack, token_inputs
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = StackConfig(n_layers=args.layers, seed=0, gate_lognormal=True)
+    stack = DipStack(cfg, dev, mode="ca")
+    xc, rc = token_inputs(cfg, 32, seed=2000, device=dev)
+    stack.calibrate_ca(xc, rc)
+    T = args.warmup + args.steps
+    x0, resid = token_inputs(cfg, T, seed=1000, device=dev)
+    ms_ca, clk = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
+    # hit rate and split exactness over recorded eager tokens
+    hits, exact, n_tok = 0, True, min(8, args.steps)
+    for t in range(n_tok):
+        stack.step(x0[t], resid[t], record=True)
+        for l, (idx, (comb, src, row, n_hit)) in enumerate(zip(stack.last_idx, stack.last_split)):
+            id2 = stack.ca[l]["id2slot"]
+            il = idx.long()
+            hitm = id2[il] >= 0
+            ref = torch.cat([il[hitm], il[~hitm]])
+            nh = int(hitm.sum())
+            ok = (torch.equal(comb.long(), ref) and int(n_hit) == nh and
+                  torch.equal(src.long(), torch.cat([torch.zeros(nh, dtype=torch.long, device=dev),
+                                                     torch.ones(il.numel() - nh, dtype=torch.long,
+                                                                device=dev)])) and
+                  torch.equal(row.long(), torch.cat([id2[il[hitm]], il[~hitm]])))
+            exact = exact and ok
+            hits += nh
+    hit_rate = hits / (n_tok * cfg.n_layers * cfg.k)
+    stack.mode, stack.fused, stack._graph = "fused", True, None
+    ms_fused, _ = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
+    us_ca = ms_ca * 1e3 / cfg.n_layers
+    print(json.dumps({
+        "metric": "dip_ca_mlp_decode_tok_s", "value": 1e3 / ms_ca, "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_ca,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) int4 g128 weights, gate rows x LogNormal(0,1), "
+                "N(0,1) tokens)",
+        "config": {"workload": "config2: cache-aware DIP, 64-layer stack, batch 1",
+                   "layers": cfg.n_layers, "k": cfg.k, "cache_n": cfg.cache_n,
+                   "calibration": "32 N(0,1) tokens through the DIP stack"},
+        "us_per_layer": us_ca, "hit_rate": hit_rate, "split_exact": bool(exact),
+        "split_checked_tokens": n_tok,
+        "streaming_fused_us_per_layer_same_weights": ms_fused * 1e3 / cfg.n_layers,
+        "gpu_launches": args.steps * (cfg.n_layers * 5 + cfg.n_layers - 1),
+        "clocks": clk}), flush=True)
+
+
+def run_tp(args):
+    """Config 4: the stack sharded along I over the N ranks of torchrun (NCCL):
+    per layer one all-gather of g (bf16, I values) and one all-reduce of the
+    fp32 [H] partials.  All N GPUs work on the same token: `value` is the
+    token rate of that one stream (strong scaling).  `comm_us_per_layer` times
+    the same two collectives alone (graph-replayed, 64 per step); they run on
+    the compute stream, so all of it is exposed."""
+    rank, world, local = dist_env()
+    import torch.distributed as dist
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, token_inputs
+    from dip_b200.tp import TPDipStack
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(_free_port()))
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+    dist.init_process_group("nccl", device_id=dev)
+    cfg = StackConfig(n_layers=args.layers, seed=0)
+    stack = TPDipStack(cfg, dev)
+    T = args.warmup + args.steps
+    x0, resid = token_inputs(cfg, T, seed=1000, device=dev)
+    ms, clk = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
+    tt = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item()
+    # the collectives alone
+    g_loc = torch.zeros(cfg.inter // world, dtype=torch.bfloat16, device=dev)
+    g_all = torch.zeros(cfg.inter, dtype=torch.bfloat16, device=dev)
+    part = torch.zeros(cfg.hidden, dtype=torch.float32, device=dev)
+
+    def comm():
+        for _ in range(cfg.n_layers):
+            if world > 1:
+                dist.all_gather_into_tensor(g_all, g_loc)
+                dist.all_reduce(part)
+    comm_us = 0.0
+    if world > 1:
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            comm(); comm()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            comm()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ct = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        dist.all_reduce(ct, op=dist.ReduceOp.MAX)
+        comm_us = ct.item() * 1e3 / cfg.n_layers
+    layer_us = ms * 1e3 / cfg.n_layers
+    if rank == 0:
+        print(json.dumps({
+            "metric": "dip_mlp_decode_tok_s", "value": 1e3 / ms, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
+            "config": {"workload": "config4: 64-layer stack sharded along I, batch 1",
+                       "layers": cfg.n_layers, "k": cfg.k, "parallelism": f"tp{world}"},
+            "us_per_layer": layer_us, "comm_us_per_layer": comm_us,
+            "comm_frac_of_layer": comm_us / layer_us if layer_us else None,
+            "gpu_launches": args.steps * (cfg.n_layers * 5 + cfg.n_layers - 1),
+            "clocks": clk}), flush=True)
+    # Tearing the process group down after NCCL work was captured into CUDA
+    # graphs can block; every rank is done, so leave directly.
+    dist.barrier()
+    torch.cuda.synchronize()
+    sys.stdout.flush()
+    os._exit(0)
+
+
+def _free_port():
+    import socket
+    so = socket.socket()
+    so.bind(("127.0.0.1", 0))
+    port = so.getsockname()[1]
+    so.close()
+    return port
+
+
+def run_config3(args):
+    """Config 3: B independent tokens per step through the 64-layer stack
+    (per-token DIP; the gate GEMV of up to 8 tokens shares one weight pass).
+    `value` is tokens per second of the whole batch."""
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, layer_weight_bytes
+    from dip_b200.batch import BatchedDipStack
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    cfg = StackConfig(n_layers=args.layers, seed=0)
+    stack = BatchedDipStack(cfg, B, dev)
+    T = args.warmup + args.steps
+    gen = torch.Generator().manual_seed(3000)
+    x0 = torch.randn(T, B, cfg.hidden, generator=gen).to(torch.bfloat16).to(dev)
+    resid = torch.randn(T, cfg.n_layers, B, cfg.hidden, generator=gen).to(torch.bfloat16).to(dev)
+    stack.capture()
+    xi, ri = stack._static_in
+    for t in range(args.warmup):
+        xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for t in range(args.warmup, T):
+            xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    clk = clk.summary()
+    ms = e0.elapsed_time(e1) / args.steps
+    nb = layer_weight_bytes(cfg)
+    passes = (B + 7) // 8
+    layer_bytes = passes * nb["gate"] + B * (nb["up"] + nb["down"])
+    layer_us = ms * 1e3 / cfg.n_layers
+    peak, peak_kind = _peaks()
+    print(json.dumps({
+        "metric": "dip_mlp_decode_tok_s", "value": B * 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
+        "config": {"workload": f"config3: 64-layer stack, batch {B} independent tokens",
+                   "batch": B, "layers": cfg.n_layers, "k": cfg.k},
+        "us_per_layer": layer_us, "us_per_token_layer": layer_us / B,
+        "layer_bytes": layer_bytes, "layer_hbm_gbs": layer_bytes / (layer_us * 1e-6) / 1e9,
+        "layer_hbm_frac": layer_bytes / (layer_us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
+        "gpu_launches": args.steps * cfg.n_layers * (passes + 1 + 2 * B + 1),
+        "clocks": clk}), flush=True)
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     import dip_b200  # noqa: F401  (loads the kernels; raises if unbuilt)
@@ -327,6 +540,12 @@ def main():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--cpu-layers", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3],
+                    help="1: DIP stack (the headline line); 2: cache-aware DIP stack; "
+                         "3: batched decode (--batch)")
+    ap.add_argument("--batch", type=int, default=8, help="config 3: tokens per step")
+    ap.add_argument("--tp", action="store_true",
+                    help="config 4: shard every layer along I over the torchrun ranks")
     ap.add_argument("--single-layer", type=int, default=0, metavar="N",
                     help="profiling aid: N launches of one config-1 fused layer, then exit")
     ap.add_argument("--path", default="fused", choices=["fused", "chain"],
@@ -335,6 +554,12 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.single_layer:
         run_single_layer(args.single_layer)
+    elif args.config == 2:
+        run_config2(args)
+    elif args.config == 3:
+        run_config3(args)
+    elif args.tp:
+        run_tp(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

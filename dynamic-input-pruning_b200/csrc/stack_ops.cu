@@ -10,6 +10,10 @@ __global__ void __launch_bounds__(1024)
 residual_rmsnorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ r, int n,
                         float eps, uint16_t* __restrict__ out) {
   __shared__ float wsum[32];
+  // one CTA per row
+  y += (size_t)blockIdx.x * n;
+  r += (size_t)blockIdx.x * n;
+  out += (size_t)blockIdx.x * n;
   pdl_wait();
   float ss = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -41,7 +45,13 @@ using namespace dip;
 
 extern "C" int dip_residual_rmsnorm(const dip_bf16* y, const dip_bf16* r, int64_t n, float eps,
                                     dip_bf16* out, dip_stream_t stream) {
-  if (n <= 0 || n > (1 << 20) || !y || !r || !out) return DIP_ERR_ARG;
-  return launch_status(launch(residual_rmsnorm_kernel, dim3(1), dim3(1024), 0,
+  return dip_residual_rmsnorm_rows(y, r, 1, n, eps, out, stream);
+}
+
+extern "C" int dip_residual_rmsnorm_rows(const dip_bf16* y, const dip_bf16* r, int64_t rows,
+                                         int64_t n, float eps, dip_bf16* out,
+                                         dip_stream_t stream) {
+  if (n <= 0 || n > (1 << 20) || rows <= 0 || rows > 65535 || !y || !r || !out) return DIP_ERR_ARG;
+  return launch_status(launch(residual_rmsnorm_kernel, dim3((unsigned)rows), dim3(1024), 0,
                               (cudaStream_t)stream, y, r, (int)n, eps, out));
 }

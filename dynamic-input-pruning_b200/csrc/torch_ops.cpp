@@ -348,10 +348,28 @@ Tensor residual_rmsnorm(const Tensor& y_in, const Tensor& r_in, double eps) {
   check_dtype(y, at::kBFloat16, "y");
   check_dtype(r, at::kBFloat16, "r");
   TORCH_CHECK(y.numel() == r.numel(), "residual_rmsnorm: y/r size mismatch");
+  TORCH_CHECK(y.dim() == 1 || y.dim() == 2, "residual_rmsnorm: y must be [n] or [rows, n]");
   c10::cuda::CUDAGuard guard(y.device());
   Tensor out = at::empty_like(y);
-  check_status(dip_residual_rmsnorm(bf(y), bf(r), y.numel(), (float)eps, bfm(out), cur_stream()),
+  const int64_t rows = y.dim() == 2 ? y.size(0) : 1;
+  const int64_t n = y.dim() == 2 ? y.size(1) : y.numel();
+  check_status(dip_residual_rmsnorm_rows(bf(y), bf(r), rows, n, (float)eps, bfm(out), cur_stream()),
                "residual_rmsnorm");
+  return out;
+}
+
+// config 3: x [B, in] -> [B, rows] (gate GEMV with SiLU, or plain)
+Tensor gemv_batched(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, bool silu) {
+  check_packed(qweight, scales, "gemv_batched");
+  Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_dtype(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.dim() == 2 && x.size(1) == qweight.size(1) * 2, "gemv_batched: x must be [B, in]");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty({x.size(0), qweight.size(0)}, x.options());
+  check_status(dip_int4_gemv_batched(i8(qweight), bf(scales), bf(x), bfm(out), qweight.size(0),
+                                     x.size(1), x.size(0), silu ? 1 : 0, cur_stream()),
+               "gemv_batched");
   return out;
 }
 
@@ -509,6 +527,7 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
   m.def("residual_rmsnorm(Tensor y, Tensor r, float eps) -> Tensor");
+  m.def("gemv_batched(Tensor qweight, Tensor scales, Tensor x, bool silu) -> Tensor");
   m.def("shard_select(Tensor idx, int lo, int hi) -> (Tensor, Tensor)");
   m.def(
       "gather_up_h_count(Tensor up_qw, Tensor up_sc, Tensor x, Tensor g, Tensor idx, "
@@ -534,6 +553,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("dequantize_int4", &dequantize_int4);
   m.impl("transpose_down_int4", &transpose_down_int4);
   m.impl("residual_rmsnorm", &residual_rmsnorm);
+  m.impl("gemv_batched", &gemv_batched);
   m.impl("shard_select", &shard_select);
   m.impl("gather_up_h_count", &gather_up_h_count);
   m.impl("gather_down_partial", &gather_down_partial);

@@ -109,6 +109,11 @@ def _register_fakes_fused():
                 torch.empty(k, dtype=torch.int32, device=x.device))
 
 
+    @torch.library.register_fake("dip_b200::gemv_batched")
+    def _(qweight, scales, x, silu):
+        return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)
+
+
 def header_symbols() -> list[str]:
     """Every function the public header declares (DIP_API ...)."""
     import re

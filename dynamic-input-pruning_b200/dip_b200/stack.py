@@ -1,4 +1,4 @@
-"""Synthetic Qwen3-32B-shaped DIP decode stack (BASELINE configs 1 and 2).
+"""Synthetic Qwen3-32B-shaped DIP decode stack (configs 1 and 2 of the benchmark).
 
 Per layer the input is RMSNorm(prev_y + r) with unit weight, r an N(0,1) bf16
 residual; the first layer's input is an N(0,1) token.  Weights are bf16
@@ -75,51 +75,114 @@ def layer_weight_bytes(cfg: StackConfig) -> dict:
 
 
 class DipStack:
-    """A stack of resident DIP MLP layers with the synthetic inter-layer step."""
+    """A stack of resident DIP MLP layers with the synthetic inter-layer step.
+
+    mode "fused": one persistent kernel per layer (dip_mlp_decode_fused,
+    RMSNorm folded in); "chain": the separate-launch chain (dip_mlp_decode);
+    "ca": cache-aware DIP (dip_ca.py:127-188): gate + top-k, hit/miss split
+    against the layer's resident hot set, dual-source up and down.  The "ca"
+    mode needs calibrate_ca() first."""
 
     def __init__(self, cfg: StackConfig, device="cuda:0", layers: list | None = None,
-                 fused: bool = True):
+                 fused: bool = True, mode: str | None = None):
         self.cfg = cfg
-        # fused: one persistent kernel per layer (dip_mlp_decode_fused, RMSNorm
-        # folded in); otherwise the separate-launch chain (dip_mlp_decode).
-        self.fused = fused
+        self.mode = mode if mode is not None else ("fused" if fused else "chain")
+        if self.mode not in ("fused", "chain", "ca"):
+            raise ValueError(f"unknown mode {self.mode!r}")
+        self.fused = self.mode == "fused"
         self.device = torch.device(device)
         self.layers = layers if layers is not None else [
             make_layer(cfg, l, self.device) for l in range(cfg.n_layers)]
         self._graph = None
         self._static_in = None
         self._static_out = None
-        # Last token's per-layer selections (filled by decode_eager).
+        # Last token's per-layer selections and CA splits (filled when recording).
         self.last_idx = None
+        self.last_split = None
+        self.ca = None  # per layer: id2slot, cache_ids and resident rows
+
+    # -- cache-aware DIP ---------------------------------------------------
+    def calibrate_ca(self, x0s: torch.Tensor, resids: torch.Tensor) -> list:
+        """Runs the tokens x0s [T, H] (residuals [T, L, H]) through the DIP
+        stack, counts every layer's selected channels (as the reference's hook
+        does, dip_ca.py:272-300) and loads each layer's hot set: the top
+        cache_n channels by (count desc, id asc), kept sorted ascending, with
+        id2slot[id] = rank and resident copies of their up / down rows
+        (dip_ca.py:107-117).  Returns the per-layer counts."""
+        from .dip_ca import _hot_order
+        saved = self.mode
+        self.mode, self.fused = "fused", True
+        cnt = [torch.zeros(self.cfg.inter, dtype=torch.long, device=self.device)
+               for _ in self.layers]
+        try:
+            for t in range(x0s.shape[0]):
+                self.step(x0s[t].to(self.device), resids[t].to(self.device), record=True)
+                for l, idx in enumerate(self.last_idx):
+                    i = idx.long()
+                    cnt[l].index_add_(0, i, torch.ones_like(i))
+        finally:
+            self.mode, self.fused = saved, saved == "fused"
+        self.ca = []
+        for l, L in enumerate(self.layers):
+            hot = _hot_order(cnt[l], self.cfg.inter)[: self.cfg.cache_n].sort().values
+            id2 = torch.full((self.cfg.inter,), -1, dtype=torch.long, device=self.device)
+            id2[hot] = torch.arange(len(hot), device=self.device)
+            self.ca.append({"cache_ids": hot, "id2slot": id2,
+                            "res_up_qw": L["up_qw"][hot].contiguous(),
+                            "res_up_sc": L["up_sc"][hot].contiguous(),
+                            "res_dn_qw": L["down_t_qw"][hot].contiguous(),
+                            "res_dn_sc": L["down_t_sc"][hot].contiguous()})
+        self._graph = None
+        return cnt
 
     # -- one token, eager -------------------------------------------------
     def step(self, x0: torch.Tensor, resid: torch.Tensor, record: bool = False) -> torch.Tensor:
         """x0 [hidden] bf16, resid [n_layers, hidden] bf16 -> last layer's y."""
         k = self.cfg.k
-        if getattr(self, "_ws", None) is None or self._ws.device != x0.device:
+        if self.mode != "ca" and (getattr(self, "_ws", None) is None
+                                  or self._ws.device != x0.device
+                                  or getattr(self, "_ws_mode", None) != self.mode):
             op = (torch.ops.dip_b200.mlp_fused_workspace_bytes if self.fused
                   else torch.ops.dip_b200.mlp_workspace_bytes)
             nb = op(self.cfg.hidden, self.cfg.inter, k)
             # zeroed once; every decode call leaves it reusable
             self._ws = torch.zeros(nb, dtype=torch.uint8, device=x0.device)
-        idxs = []
+            self._ws_mode = self.mode
+        if self.mode == "ca" and self.ca is None:
+            raise RuntimeError("cache-aware mode needs calibrate_ca() first")
+        idxs, splits = [], []
         y = None
         for l, L in enumerate(self.layers):
-            if self.fused:
+            if self.mode == "fused":
                 xin, r = (x0, None) if l == 0 else (y, resid[l])
                 y, g, idx = torch.ops.dip_b200.mlp_decode_fused(
                     L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
                     L["down_t_sc"], xin, r, RMS_EPS, k, self._ws)
             else:
                 x = x0 if l == 0 else torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
-                y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"],
-                                                          L["up_qw"], L["up_sc"],
-                                                          L["down_t_qw"], L["down_t_sc"], x, k,
-                                                          self._ws)
+                if self.mode == "chain":
+                    y, g, idx = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"],
+                                                              L["up_qw"], L["up_sc"],
+                                                              L["down_t_qw"], L["down_t_sc"],
+                                                              x, k, self._ws)
+                else:
+                    C = self.ca[l]
+                    g = torch.ops.dip_b200.gate_silu(L["gate_qw"], L["gate_sc"], x)
+                    idx = torch.ops.topk_ops.topk_select(g, k)
+                    comb, src, row, n_hit = torch.ops.dip_b200.ca_split(idx, C["id2slot"])
+                    h = torch.ops.dip_b200.srcrow_up_h(C["res_up_qw"], C["res_up_sc"],
+                                                       L["up_qw"], L["up_sc"], x, g, comb, src,
+                                                       row)
+                    y = torch.ops.dip_b200.srcrow_down(C["res_dn_qw"], C["res_dn_sc"],
+                                                       L["down_t_qw"], L["down_t_sc"], h, src,
+                                                       row)
+                    if record:
+                        splits.append((comb, src, row, n_hit))
             if record:
                 idxs.append(idx)
         if record:
             self.last_idx = idxs
+            self.last_split = splits if self.mode == "ca" else None
         return y
 
     # -- one token, CUDA graph --------------------------------------------

@@ -88,3 +88,59 @@ class TPDipMlp:
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         self.last_idx = idx
         return y.to(torch.bfloat16)
+
+
+class TPDipStack:
+    """Config 4: the synthetic 64-layer stack (dip_b200.stack) with every layer
+    sharded along I over the process group.  Each rank generates a layer's full
+    weights from the same seed, keeps its shard and frees the rest.  The
+    inter-layer step (RMSNorm(y + r)) runs replicated on every rank on the
+    all-reduced y, so all ranks see identical inputs."""
+
+    def __init__(self, cfg, device, group=None):
+        from .stack import make_layer
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        self.mlps = []
+        for l in range(cfg.n_layers):
+            full = make_layer(cfg, l, self.device)
+            self.mlps.append(TPDipMlp(shard_layer(full, rank, world), cfg.k, group))
+            del full
+        torch.cuda.empty_cache()
+        self._graph = None
+        self._static_in = None
+        self._static_out = None
+        self.last_idx = None
+
+    def step(self, x0, resid, record=False):
+        from .stack import RMS_EPS
+        y, idxs = None, []
+        for l, m in enumerate(self.mlps):
+            x = x0 if l == 0 else torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
+            y = m.decode_token(x)
+            if record:
+                idxs.append(m.last_idx)
+        if record:
+            self.last_idx = idxs
+        return y
+
+    def capture(self):
+        H, n = self.cfg.hidden, self.cfg.n_layers
+        self._static_in = (torch.zeros(H, dtype=torch.bfloat16, device=self.device),
+                           torch.zeros(n, H, dtype=torch.bfloat16, device=self.device))
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # collectives and kernels initialised before capture
+                self.step(*self._static_in)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._static_out = self.step(*self._static_in)
+        self._graph = g
+
+    def replay(self):
+        self._graph.replay()
+        return self._static_out

@@ -73,6 +73,18 @@ DIP_API int dip_int4_gemv(const int8_t* qweight, const dip_bf16* scales, const d
                   dip_bf16* out, int64_t rows, int64_t in_features, int apply_silu,
                   dip_stream_t stream);
 
+/* ---- config 3: the same GEMV for a batch of tokens -------------------------
+ * out[t, r] = bf16(sum_c q[r,c]*s[r,c/128]*x[t,c]) for t < ntok (x [ntok, in],
+ * out [ntok, rows], both row-major); with apply_silu != 0 then bf16(silu(.)).
+ * Each token's result equals dip_int4_gemv's bit for bit.  One pass over the
+ * weights serves 8 tokens (the 8 columns of the tensor-core tile); larger
+ * batches take ceil(ntok / 8) passes.  Replaces the per-token gate GEMV of
+ * the batch loop (dip_stream_predispatch.py:166-174 per token).  in_features
+ * must be a multiple of 1024; 16-byte aligned pointers. */
+DIP_API int dip_int4_gemv_batched(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
+                                  dip_bf16* out, int64_t rows, int64_t in_features, int64_t ntok,
+                                  int apply_silu, dip_stream_t stream);
+
 /* ---- a7: top-k of |s| -------------------------------------------------------
  * Exactly the selection of topk_ops::topk_select
  * (kernels/topk_select/topk_select.cu:134-164): 25-step fp32 bisection on
@@ -260,6 +272,10 @@ DIP_API int dip_gather_down_partial(const int8_t* down_t, const dip_bf16* scales
  * MLP; it defines the per-layer inputs of the 64-layer benchmark stack. */
 DIP_API int dip_residual_rmsnorm(const dip_bf16* y, const dip_bf16* r, int64_t n, float eps,
                                  dip_bf16* out, dip_stream_t stream);
+/* The same for `rows` consecutive rows of n values (one normalisation per
+ * row): the batched stack's per-token inter-layer step. */
+DIP_API int dip_residual_rmsnorm_rows(const dip_bf16* y, const dip_bf16* r, int64_t rows, int64_t n,
+                                      float eps, dip_bf16* out, dip_stream_t stream);
 
 #ifdef __cplusplus
 }
