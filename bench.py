@@ -196,10 +196,10 @@ def run_config2(args):
     """Config 2: cache-aware DIP on the 64-layer stack with LogNormal(0,1)
     gate-row scales; calibration on 32 N(0,1) tokens run through the DIP
     stack, cache_n = 0.3 I hot channels per layer.  Reports us/layer and
-    tok/s of the CA path (and of the streaming fused path on the same
-    weights), the hit rate, and whether every recorded hit/miss split equals
-    its definition (hits then misses, each in top-k order) recomputed with
-    torch ops from the same indices."""
+    tok/s of the one-launch CA layer (and of the separate-launch CA chain and
+    the streaming fused layer on the same weights), the hit rate, and whether
+    every recorded hit/miss split equals its definition (hits then misses,
+    each in top-k order) recomputed with torch ops from the same indices."""
     import dip_b200  # noqa: F401
     from dip_b200.stack import StackConfig, DipStack, token_inputs
     dev = torch.device("cuda", 0)
@@ -229,6 +229,8 @@ def run_config2(args):
             exact = exact and ok
             hits += nh
     hit_rate = hits / (n_tok * cfg.n_layers * cfg.k)
+    stack.mode, stack.fused, stack._graph = "ca_chain", False, None
+    ms_chain, _ = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
     stack.mode, stack.fused, stack._graph = "fused", True, None
     ms_fused, _ = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
     us_ca = ms_ca * 1e3 / cfg.n_layers
@@ -243,8 +245,9 @@ def run_config2(args):
                    "calibration": "32 N(0,1) tokens through the DIP stack"},
         "us_per_layer": us_ca, "hit_rate": hit_rate, "split_exact": bool(exact),
         "split_checked_tokens": n_tok,
+        "ca_separate_launches_us_per_layer": ms_chain * 1e3 / cfg.n_layers,
         "streaming_fused_us_per_layer_same_weights": ms_fused * 1e3 / cfg.n_layers,
-        "gpu_launches": args.steps * (cfg.n_layers * 5 + cfg.n_layers - 1),
+        "gpu_launches": args.steps * cfg.n_layers,
         "clocks": clk}), flush=True)
 
 

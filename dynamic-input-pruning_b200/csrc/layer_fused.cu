@@ -83,6 +83,11 @@ struct LfArgs {
   float* y_f32;             // optional
   GridBar* bar;
   unsigned* err;
+  // cache-aware DIP (dip_ca.py:127-188), optional: channel c's up and down
+  // rows come from the resident cache row id2slot[c] when that is >= 0
+  const int64_t* id2slot;
+  const uint8_t* res_up_qw; const uint16_t* res_up_sc;
+  const uint8_t* res_dn_qw; const uint16_t* res_dn_sc;
 };
 
 // Byte offsets of the dynamic shared memory.
@@ -103,7 +108,8 @@ struct LfGeom {
   static constexpr int red = gsum + ((G * 4 + 15) & ~15);  // [tiles][warps][16]
   static constexpr int red_words = (kLfTilesA + 1) * kLfWarps * 16;
   static constexpr int gloc = red + red_words * 4;         // this CTA's g values (bf16)
-  static constexpr int misc = gloc + kLfListMax * 2;       // small scalars
+  static constexpr int lslot = gloc + kLfListMax * 2;      // this CTA's cache slots (CA-DIP)
+  static constexpr int misc = lslot + kLfListMax * 4;      // small scalars
   static constexpr int total = misc + 256;
 };
 
@@ -169,34 +175,33 @@ __device__ __forceinline__ void lf_tile_dot(const uint8_t* slot, const uint32_t 
 }
 
 // Issue one GEMV tile slice into this warp's ring slot: groups [warp*GW,
-// (warp+1)*GW) of the tile's 16 rows (row(r) gives the row index of tile row
-// r), plus the 4-byte scale words of the 16 rows (lanes 0..15).  Slot layout
+// (warp+1)*GW) of the tile's 16 rows (qrow(r) / srow(r) give tile row r's
+// packed row and scale row), plus the 4-byte scale words of the 16 rows
+// (lanes 0..15).  Slot layout
 // (read by lf_tile_dot): [group gi][rows 0-7 | rows 8-15][lane (row&7)*4 + tq]
 // x 16 bytes.  With GW == 2 a warp's slice of a row is one aligned 128-byte
 // line, so each instruction fetches 4 whole lines (8 lanes per row); with
 // GW == 1 it is 64 bytes (4 lanes per row, 8 rows per instruction).
-template <int GW, class RowFn>
-__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, const uint8_t* base, const uint16_t* sbase,
-                                              int rowb, int scw, RowFn row, int warp, int lane) {
+template <int GW, class QRow, class SRow>
+__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, QRow qrow, SRow srow, int warp, int lane) {
   if (GW == 2) {
     const int rsub = lane >> 3, c = lane & 7, gi = c >> 2, tq = c & 3;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int r = 4 * j + rsub;
       cp_async16_lf(slot + (gi * 2 + (r >> 3)) * 512 + ((r & 7) * 4 + tq) * 16,
-                    base + (size_t)row(r) * rowb + warp * 128 + c * 16);
+                    qrow(r) + warp * 128 + c * 16);
     }
   } else {
     const int gq = lane >> 2, tq = lane & 3;
     const int off = warp * kGroupBytes + tq * 16;
-    cp_async16_lf(slot + lane * 16, base + (size_t)row(gq) * rowb + off);
-    cp_async16_lf(slot + 512 + lane * 16, base + (size_t)row(gq + 8) * rowb + off);
+    cp_async16_lf(slot + lane * 16, qrow(gq) + off);
+    cp_async16_lf(slot + 512 + lane * 16, qrow(gq + 8) + off);
   }
   if (lane < 16) {
     // GW == 2: the 4 bytes [4 warp, 4 warp + 4); GW == 1: 2 bytes, copy the
     // aligned 4-byte word containing them.
-    const uint16_t* p = sbase + (size_t)row(lane) * scw + ((warp * GW) & ~1);
-    cp_async4_lf(slot + GW * 1024 + lane * 4, p);
+    cp_async4_lf(slot + GW * 1024 + lane * 4, srow(lane) + ((warp * GW) & ~1));
   }
 }
 
@@ -435,7 +440,7 @@ __device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* s
   LF_CTA(22);
 }
 
-template <int GW>
+template <int GW, bool CA>
 __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs a) {
   using Geo = LfGeom<GW>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -469,8 +474,10 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   auto issue_a = [&](int i) {
     if (i < nta) {
       const int rbase = ra0 + i * 16, rlast = ra1 - 1;
-      lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.gate_qw, a.gate_sc, rowb, scw,
-                        [&](int r) { return min(rbase + r, rlast); }, warp, lane);
+      lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot,
+                        [&](int r) { return a.gate_qw + (size_t)min(rbase + r, rlast) * rowb; },
+                        [&](int r) { return a.gate_sc + (size_t)min(rbase + r, rlast) * scw; },
+                        warp, lane);
     }
     cp_commit_lf();
   };
@@ -581,6 +588,13 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     a.g[ra0 + r] = o;
     gloc[r] = o;
   }
+  {
+    // cache slots of this CTA's rows (-1: no cache), loaded by the threads
+    // the loop above leaves idle
+    int* lslot_w = reinterpret_cast<int*>(smem + Geo::lslot);
+    const int t = tid - (kLfThreads - 16 * kLfTilesA);
+    if (CA && t >= 0 && t < na) lslot_w[t] = (int)a.id2slot[ra0 + t];
+  }
   __syncthreads();
   // |g| histograms, aggregated over the CTA first in shared memory (the ring,
   // idle now): SiLU's minimum piles ~1/8 of all values into two or three fine
@@ -663,10 +677,23 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   __shared__ int s_n[2];
   int nC = nts, nD = 0, nDA = 0;
   bool have1 = false, have2 = false;
+  // Row sources: channel ch (one of this CTA's rows) reads its up / down row
+  // from the resident cache when it has a slot there, else from the full
+  // matrices.
+  const int* lslot = reinterpret_cast<const int*>(smem + Geo::lslot);
+  auto slot_of = [&](int ch) { return CA ? lslot[ch - ra0] : -1; };
+  auto up_q = [&](int ch) {
+    const int sl = slot_of(ch);
+    return sl >= 0 ? a.res_up_qw + (size_t)sl * rowb : a.up_qw + (size_t)ch * rowb;
+  };
+  auto up_s = [&](int ch) {
+    const int sl = slot_of(ch);
+    return sl >= 0 ? a.res_up_sc + (size_t)sl * scw : a.up_sc + (size_t)ch * scw;
+  };
   auto issue_c = [&](int i) {
     const int* rp = crow + i * 16;
-    lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, a.up_qw, a.up_sc, rowb, scw,
-                      [&](int r) { return rp[r]; }, warp, lane);
+    lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, [&](int r) { return up_q(rp[r]); },
+                      [&](int r) { return up_s(rp[r]); }, warp, lane);
   };
   const int seg = warp * GW * kGroupBytes;
   auto issue_d = [&](int j) {  // j: stream index; D tile j - nC
@@ -677,11 +704,15 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       const int chk = lane + 32 * q;
       const int r = chk / (GW * 4), part = chk % (GW * 4);
       const int ch = drow[i * 16 + r];
-      cp_async16_lf(slot + r * kLfDnPitch + part * 16, a.dn_qw + (size_t)ch * rowb + seg + part * 16);
+      const int sl = slot_of(ch);
+      const uint8_t* row = sl >= 0 ? a.res_dn_qw + (size_t)sl * rowb : a.dn_qw + (size_t)ch * rowb;
+      cp_async16_lf(slot + r * kLfDnPitch + part * 16, row + seg + part * 16);
     }
     if (lane < 16) {
       const int ch = drow[i * 16 + lane];
-      cp_async4_lf(slot + 16 * kLfDnPitch + lane * 4, a.dn_sc + (size_t)ch * scw + ((warp * GW) & ~1));
+      const int sl = slot_of(ch);
+      const uint16_t* srow = sl >= 0 ? a.res_dn_sc + (size_t)sl * scw : a.dn_sc + (size_t)ch * scw;
+      cp_async4_lf(slot + 16 * kLfDnPitch + lane * 4, srow + ((warp * GW) & ~1));
     }
   };
   auto issue = [&](int j) {
@@ -992,6 +1023,18 @@ size_t layer_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
 
 }  // namespace dip
 
+namespace dip {
+template <int GW, bool CA>
+static int lf_launch(const LfArgs& a, int nb, dip_stream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(layer_fused_kernel<GW, CA>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       LfGeom<GW>::total);
+  if (e != cudaSuccess) return launch_status(e);
+  return launch_status(launch_coop(layer_fused_kernel<GW, CA>, dim3(nb), dim3(kLfThreads),
+                                   (size_t)LfGeom<GW>::total, (cudaStream_t)stream, a));
+}
+}  // namespace dip
+
 using namespace dip;
 
 extern "C" size_t dip_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
@@ -1006,7 +1049,22 @@ extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, con
                                     float eps, int64_t k, void* workspace, size_t workspace_bytes,
                                     dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
                                     dip_bf16* x_used, dip_stream_t stream) {
+  return dip_mlp_decode_fused_ca(L, nullptr, x, resid, eps, k, workspace, workspace_bytes, y, g_out,
+                                 idx_out, x_used, stream);
+}
+
+extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_t* cache,
+                                       const dip_bf16* x, const dip_bf16* resid, float eps,
+                                       int64_t k, void* workspace, size_t workspace_bytes,
+                                       dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
+                                       dip_bf16* x_used, dip_stream_t stream) {
   if (!L || !x || !y || !workspace) return DIP_ERR_ARG;
+  if (cache && (!cache->id2slot || !cache->res_up_qw || !cache->res_up_sc || !cache->res_dn_qw ||
+                !cache->res_dn_sc))
+    return DIP_ERR_ARG;
+  if (cache && ((reinterpret_cast<uintptr_t>(cache->res_up_qw) |
+                 reinterpret_cast<uintptr_t>(cache->res_dn_qw)) & 15))
+    return DIP_ERR_ARG;
   const int64_t H = L->hidden, I = L->inter;
   if (k < 1 || k > I || H <= 0 || I <= 0) return DIP_ERR_ARG;
   const int nb = num_sms();
@@ -1054,17 +1112,14 @@ extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, con
   a.y = y;
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
-  cudaError_t e;
-  if (gw == 1) {
-    e = cudaFuncSetAttribute(layer_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             LfGeom<1>::total);
-    if (e != cudaSuccess) return launch_status(e);
-    return launch_status(launch_coop(layer_fused_kernel<1>, dim3(nb), dim3(kLfThreads),
-                                     (size_t)LfGeom<1>::total, (cudaStream_t)stream, a));
+  if (cache) {
+    a.id2slot = cache->id2slot;
+    a.res_up_qw = reinterpret_cast<const uint8_t*>(cache->res_up_qw);
+    a.res_up_sc = cache->res_up_sc;
+    a.res_dn_qw = reinterpret_cast<const uint8_t*>(cache->res_dn_qw);
+    a.res_dn_sc = cache->res_dn_sc;
   }
-  e = cudaFuncSetAttribute(layer_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           LfGeom<2>::total);
-  if (e != cudaSuccess) return launch_status(e);
-  return launch_status(launch_coop(layer_fused_kernel<2>, dim3(nb), dim3(kLfThreads),
-                                   (size_t)LfGeom<2>::total, (cudaStream_t)stream, a));
+  const bool ca = cache != nullptr;
+  if (gw == 1) return ca ? lf_launch<1, true>(a, nb, stream) : lf_launch<1, false>(a, nb, stream);
+  return ca ? lf_launch<2, true>(a, nb, stream) : lf_launch<2, false>(a, nb, stream);
 }

@@ -426,10 +426,10 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
   return y;
 }
 
-std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
+std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
     const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
-    const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
-    double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
+    const Tensor& dt_qw, const Tensor& dt_sc, const dip_ca_cache_t* cache, const Tensor& x_in,
+    const std::optional<Tensor>& resid, double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
   check_packed(gate_qw, gate_sc, "mlp_decode_fused(gate)");
   check_packed(up_qw, up_sc, "mlp_decode_fused(up)");
   check_packed(dt_qw, dt_sc, "mlp_decode_fused(down_t)");
@@ -454,11 +454,40 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
   Tensor ws = ws_opt.has_value() ? *ws_opt : at::zeros({(int64_t)wsb}, x.options().dtype(at::kByte));
   TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && (size_t)ws.nbytes() >= wsb,
               "mlp_decode_fused: workspace too small (need ", wsb, " bytes)");
-  check_status(dip_mlp_decode_fused(&L, bf(x), resid.has_value() ? bf(r) : nullptr, (float)eps, k,
-                                    ws.data_ptr(), wsb, bfm(y), bfm(g), idx.data_ptr<int32_t>(),
-                                    nullptr, cur_stream()),
+  check_status(dip_mlp_decode_fused_ca(&L, cache, bf(x), resid.has_value() ? bf(r) : nullptr,
+                                       (float)eps, k, ws.data_ptr(), wsb, bfm(y), bfm(g),
+                                       idx.data_ptr<int32_t>(), nullptr, cur_stream()),
                "mlp_decode_fused");
   return {y, g, idx};
+}
+
+std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
+    const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
+    const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
+    double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
+  return mlp_decode_fused_impl(gate_qw, gate_sc, up_qw, up_sc, dt_qw, dt_sc, nullptr, x_in, resid,
+                               eps, k, ws_opt);
+}
+
+// the cache-aware layer in one launch (dip_mlp_decode_fused_ca)
+std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_ca(
+    const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
+    const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& id2slot, const Tensor& res_up_qw,
+    const Tensor& res_up_sc, const Tensor& res_dn_qw, const Tensor& res_dn_sc, const Tensor& x_in,
+    const std::optional<Tensor>& resid, double eps, int64_t k,
+    const std::optional<Tensor>& ws_opt) {
+  TORCH_CHECK(id2slot.is_cuda() && id2slot.scalar_type() == at::kLong && id2slot.is_contiguous() &&
+                  id2slot.numel() == gate_qw.size(0),
+              "mlp_decode_fused_ca: id2slot must be a contiguous CUDA int64 [inter] tensor");
+  check_packed(res_up_qw, res_up_sc, "mlp_decode_fused_ca(res_up)");
+  check_packed(res_dn_qw, res_dn_sc, "mlp_decode_fused_ca(res_dn)");
+  TORCH_CHECK(res_up_qw.size(1) == up_qw.size(1) && res_dn_qw.size(1) == dt_qw.size(1) &&
+                  res_up_qw.size(0) == res_dn_qw.size(0),
+              "mlp_decode_fused_ca: cache shape mismatch");
+  dip_ca_cache_t c = {id2slot.data_ptr<int64_t>(), i8(res_up_qw), bf(res_up_sc), i8(res_dn_qw),
+                      bf(res_dn_sc), res_up_qw.size(0)};
+  return mlp_decode_fused_impl(gate_qw, gate_sc, up_qw, up_sc, dt_qw, dt_sc, &c, x_in, resid, eps,
+                               k, ws_opt);
 }
 
 int64_t op_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
@@ -523,6 +552,11 @@ TORCH_LIBRARY(dip_b200, m) {
       "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
       "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
   m.def("mlp_fused_workspace_bytes(int hidden, int inter, int k) -> int");
+  m.def(
+      "mlp_decode_fused_ca(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
+      "Tensor down_t_qw, Tensor down_t_sc, Tensor id2slot, Tensor res_up_qw, Tensor res_up_sc, "
+      "Tensor res_dn_qw, Tensor res_dn_sc, Tensor x, Tensor? resid, float eps, int k, "
+      "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
   m.def("quantize_int4(Tensor w) -> (Tensor, Tensor)");
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
@@ -549,6 +583,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("srcrow_down", &srcrow_down);
   m.impl("mlp_decode", &mlp_decode);
   m.impl("mlp_decode_fused", &mlp_decode_fused);
+  m.impl("mlp_decode_fused_ca", &mlp_decode_fused_ca);
   m.impl("quantize_int4", &quantize_int4);
   m.impl("dequantize_int4", &dequantize_int4);
   m.impl("transpose_down_int4", &transpose_down_int4);

@@ -109,6 +109,12 @@ def _register_fakes_fused():
                 torch.empty(k, dtype=torch.int32, device=x.device))
 
 
+    @torch.library.register_fake("dip_b200::mlp_decode_fused_ca")
+    def _(gq, gs, uq, us, dq, ds, id2slot, ruq, rus, rdq, rds, x, resid, eps, k, workspace=None):
+        return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
+                torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
+                torch.empty(k, dtype=torch.int32, device=x.device))
+
     @torch.library.register_fake("dip_b200::gemv_batched")
     def _(qweight, scales, x, silu):
         return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)

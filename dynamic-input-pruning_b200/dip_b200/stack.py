@@ -79,15 +79,17 @@ class DipStack:
 
     mode "fused": one persistent kernel per layer (dip_mlp_decode_fused,
     RMSNorm folded in); "chain": the separate-launch chain (dip_mlp_decode);
-    "ca": cache-aware DIP (dip_ca.py:127-188): gate + top-k, hit/miss split
-    against the layer's resident hot set, dual-source up and down.  The "ca"
-    mode needs calibrate_ca() first."""
+    "ca": cache-aware DIP (dip_ca.py:127-188) in one launch per layer
+    (dip_mlp_decode_fused_ca: hits read the layer's resident hot rows, misses
+    the full matrices); "ca_chain": the same as separate launches (gate, top-k,
+    hit/miss split, dual-source up and down).  The CA modes need calibrate_ca()
+    first; recording steps also return each layer's split."""
 
     def __init__(self, cfg: StackConfig, device="cuda:0", layers: list | None = None,
                  fused: bool = True, mode: str | None = None):
         self.cfg = cfg
         self.mode = mode if mode is not None else ("fused" if fused else "chain")
-        if self.mode not in ("fused", "chain", "ca"):
+        if self.mode not in ("fused", "chain", "ca", "ca_chain"):
             raise ValueError(f"unknown mode {self.mode!r}")
         self.fused = self.mode == "fused"
         self.device = torch.device(device)
@@ -139,16 +141,17 @@ class DipStack:
     def step(self, x0: torch.Tensor, resid: torch.Tensor, record: bool = False) -> torch.Tensor:
         """x0 [hidden] bf16, resid [n_layers, hidden] bf16 -> last layer's y."""
         k = self.cfg.k
-        if self.mode != "ca" and (getattr(self, "_ws", None) is None
-                                  or self._ws.device != x0.device
-                                  or getattr(self, "_ws_mode", None) != self.mode):
-            op = (torch.ops.dip_b200.mlp_fused_workspace_bytes if self.fused
+        fused_ws = self.mode in ("fused", "ca")
+        if self.mode != "ca_chain" and (getattr(self, "_ws", None) is None
+                                        or self._ws.device != x0.device
+                                        or getattr(self, "_ws_fused", None) != fused_ws):
+            op = (torch.ops.dip_b200.mlp_fused_workspace_bytes if fused_ws
                   else torch.ops.dip_b200.mlp_workspace_bytes)
             nb = op(self.cfg.hidden, self.cfg.inter, k)
             # zeroed once; every decode call leaves it reusable
             self._ws = torch.zeros(nb, dtype=torch.uint8, device=x0.device)
-            self._ws_mode = self.mode
-        if self.mode == "ca" and self.ca is None:
+            self._ws_fused = fused_ws
+        if self.mode in ("ca", "ca_chain") and self.ca is None:
             raise RuntimeError("cache-aware mode needs calibrate_ca() first")
         idxs, splits = [], []
         y = None
@@ -158,6 +161,15 @@ class DipStack:
                 y, g, idx = torch.ops.dip_b200.mlp_decode_fused(
                     L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
                     L["down_t_sc"], xin, r, RMS_EPS, k, self._ws)
+            elif self.mode == "ca":
+                C = self.ca[l]
+                xin, r = (x0, None) if l == 0 else (y, resid[l])
+                y, g, idx = torch.ops.dip_b200.mlp_decode_fused_ca(
+                    L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
+                    L["down_t_sc"], C["id2slot"], C["res_up_qw"], C["res_up_sc"],
+                    C["res_dn_qw"], C["res_dn_sc"], xin, r, RMS_EPS, k, self._ws)
+                if record:
+                    splits.append(torch.ops.dip_b200.ca_split(idx, C["id2slot"]))
             else:
                 x = x0 if l == 0 else torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
                 if self.mode == "chain":
@@ -182,7 +194,7 @@ class DipStack:
                 idxs.append(idx)
         if record:
             self.last_idx = idxs
-            self.last_split = splits if self.mode == "ca" else None
+            self.last_split = splits if self.mode in ("ca", "ca_chain") else None
         return y
 
     # -- one token, CUDA graph --------------------------------------------

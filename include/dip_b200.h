@@ -232,6 +232,29 @@ DIP_API int dip_mlp_decode_fused(const dip_layer_t* layer, const dip_bf16* x,
                                  size_t workspace_bytes, dip_bf16* y, dip_bf16* g_out,
                                  int32_t* idx_out, dip_bf16* x_used, dip_stream_t stream);
 
+/* ---- a11 + a12/a13, one launch: the cache-aware layer --------------------------
+ * dip_mlp_decode_fused with the cache-aware DIP split of dip_ca.py:127-188
+ * folded into the row reads: selected channel c reads its up and down rows
+ * from row id2slot[c] of the resident cache when id2slot[c] >= 0 (a hit),
+ * else from the full matrices (a miss).  Every channel's rows are the same
+ * bytes either way, so y, g and idx equal dip_mlp_decode_fused's; the split
+ * itself (hits then misses, dip_ca_split) is not materialised.  The cache
+ * arrays have the layer's row formats (up [n_res, hidden/2] + scales, down_t
+ * [n_res, hidden/2] + scales); 16-byte aligned. */
+typedef struct dip_ca_cache {
+  const int64_t* id2slot;     /* [inter], -1 = not cached */
+  const int8_t* res_up_qw;    /* [n_res, hidden/2] */
+  const dip_bf16* res_up_sc;  /* [n_res, hidden/128] */
+  const int8_t* res_dn_qw;    /* [n_res, hidden/2] (transposed down rows) */
+  const dip_bf16* res_dn_sc;  /* [n_res, hidden/128] */
+  int64_t n_res;
+} dip_ca_cache_t;
+DIP_API int dip_mlp_decode_fused_ca(const dip_layer_t* layer, const dip_ca_cache_t* cache,
+                                    const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
+                                    void* workspace, size_t workspace_bytes, dip_bf16* y,
+                                    dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
+                                    dip_stream_t stream);
+
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit
  * exact with scripts/quantize.py:32-64. */

@@ -109,3 +109,12 @@ def test_modules_importable(dip):
     assert dip.StreamingDIPMlp and dip.CADIPMlp and dip.QuantLinear
     from dip_b200 import dip_stream_predispatch as dsp
     assert dsp._use_gather and dsp._use_down
+
+
+def test_python_modules_import():
+    """Every module of the package imports on a host without a GPU (the
+    kernels load; nothing runs)."""
+    import importlib
+    for m in ("dip_b200.stack", "dip_b200.batch", "dip_b200.tp", "dip_b200.dip_ca",
+              "dip_b200.dip_stream_predispatch", "dip_b200.qlinear"):
+        importlib.import_module(m)

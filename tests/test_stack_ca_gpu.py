@@ -1,18 +1,21 @@
 """Cache-aware DIP in the synthetic stack (config 2 at reduced size, GPU):
 after calibration every layer's hot set follows the reference's ordering
-(count desc, id asc) and the CA step selects the same channels as the
-streaming step, with y equal up to summation order."""
+(count desc, id asc), every split equals the oracle's, and the CA step
+selects the same channels as the streaming step of the same kind (one
+launch per layer, or separate launches), with y equal up to summation
+order."""
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
 
-def test_ca_stack_matches_streaming(dip, oracle):
+@pytest.mark.parametrize("mode", ["ca", "ca_chain"])
+def test_ca_stack_matches_streaming(dip, oracle, mode):
     from dip_b200.stack import StackConfig, DipStack, token_inputs
     dev = torch.device("cuda", 0)
     cfg = StackConfig(n_layers=3, hidden=2560, inter=8192, seed=5, gate_lognormal=True)
-    st = DipStack(cfg, dev, mode="ca")
+    st = DipStack(cfg, dev, mode=mode)
     xc, rc = token_inputs(cfg, 6, seed=11, device=dev)
     counts = st.calibrate_ca(xc, rc)
     for l, c in enumerate(counts):
@@ -29,14 +32,40 @@ def test_ca_stack_matches_streaming(dip, oracle):
         rc_, rs_, rr_, rn_ = oracle.ca_split(idx.cpu(), st.ca[l]["id2slot"].cpu())
         assert torch.equal(comb.cpu(), rc_) and torch.equal(src.cpu(), rs_)
         assert torch.equal(row.cpu(), rr_) and int(n_hit) == rn_
-    st.mode, st.fused = "chain", False
+    # the streaming path with the same inter-layer RMSNorm code: in-kernel for
+    # the one-launch layers, the separate kernel for the chains
+    st.mode = "fused" if mode == "ca" else "chain"
+    st.fused = st.mode == "fused"
     y_st = st.step(x0[1], r[1], record=True)
     for a, b in zip(idx_ca, st.last_idx):
         assert torch.equal(a, b)
     err = (y_ca.float() - y_st.float()).abs().max().item()
     assert err <= 1e-2 * y_st.float().abs().max().item() + 2e-3
     # the CUDA-graph path of the CA stack gives the eager result
-    st.mode, st.fused = "ca", False
+    st.mode, st.fused = mode, False
     st._graph = None
     y_g = st.decode(x0[1], r[1])
     assert torch.equal(y_g, y_ca)
+
+
+def test_fused_ca_equals_fused_streaming(dip):
+    """The one-launch cache-aware layer reads the same bytes as the streaming
+    fused layer (hits from the cache copy, misses from the full rows), so g,
+    idx and y are identical bit for bit."""
+    from dip_b200.stack import StackConfig, make_layer
+    dev = torch.device("cuda", 0)
+    cfg = StackConfig(n_layers=1, seed=21, gate_lognormal=True)
+    L = make_layer(cfg, 0, dev)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    hot = torch.randperm(cfg.inter, generator=gen, device=dev)[: cfg.cache_n].sort().values
+    id2 = torch.full((cfg.inter,), -1, dtype=torch.long, device=dev)
+    id2[hot] = torch.arange(len(hot), device=dev)
+    res = [L["up_qw"][hot].contiguous(), L["up_sc"][hot].contiguous(),
+           L["down_t_qw"][hot].contiguous(), L["down_t_sc"][hot].contiguous()]
+    x = torch.randn(cfg.hidden, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).to(dev)
+    args = (L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"], L["down_t_sc"])
+    a = torch.ops.dip_b200.mlp_decode_fused(*args, x, None, 1e-6, cfg.k)
+    b = torch.ops.dip_b200.mlp_decode_fused_ca(*args, id2, *res, x, None, 1e-6, cfg.k)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    assert torch.ops.dip_b200.take_device_error() == 0
