@@ -16,6 +16,7 @@ import shutil
 import subprocess
 import sys
 import sysconfig
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_ROOT = Path(__file__).resolve().parent
@@ -56,12 +57,13 @@ def build_core(force: bool = False) -> Path:
         return out
     objdir = PKG_ROOT / "_build"
     objdir.mkdir(exist_ok=True)
-    objs = []
-    for s in srcs:
-        o = objdir / (s.stem + ".o")
-        _run([_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-              "-Xcompiler", "-fvisibility=hidden", "-I", str(INCLUDE), "-c", str(s), "-o", str(o)])
-        objs.append(str(o))
+    objs = [str(objdir / (s.stem + ".o")) for s in srcs]
+    cmds = [[_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+             "-Xcompiler", "-fvisibility=hidden", "-I", str(INCLUDE), "-c", str(s), "-o", o]
+            for s, o in zip(srcs, objs)]
+    # the translation units are independent: compile them concurrently
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as ex:
+        list(ex.map(_run, cmds))
     _run([_nvcc(), *ARCH, "-shared", "-o", str(out), *objs, "-lcudart"])
     return out
 

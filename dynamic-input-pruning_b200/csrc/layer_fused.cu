@@ -38,7 +38,7 @@ namespace dip {
 
 // Phase tracing (compile with -DDIP_TRACE): thread 0 of CTA 1 records the
 // global timer at phase boundaries into dip_lf_trace[]; thread 0 of every CTA
-// records its clock at the points of dip_lf_cta[][].
+// records the global timer at the points of dip_lf_cta[][].
 #ifdef DIP_TRACE
 __device__ unsigned long long dip_lf_trace[16];
 __device__ unsigned long long dip_lf_cta[160][32];
@@ -54,7 +54,8 @@ namespace dip {
   do { if (threadIdx.x == 0 && blockIdx.x == 1) { unsigned long long t; \
        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_trace[n] = t; } } while (0)
 #define LF_CTA(n) \
-  do { if (threadIdx.x == 0) { dip_lf_cta[blockIdx.x][n] = clock64(); } } while (0)
+  do { if (threadIdx.x == 0) { unsigned long long t; \
+       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_cta[blockIdx.x][n] = t; } } while (0)
 #else
 #define LF_TRACE(n) do { } while (0)
 #define LF_CTA(n) do { } while (0)
