@@ -181,7 +181,10 @@ namespace dip {
 // is bounded: after kSpinLimit polls it ORs an error code into the device
 // error word (a kernel argument, see error_word_ptr) and reports failure
 // instead of hanging.
-constexpr uint32_t kSpinLimit = 1u << 24;
+#ifndef DIP_SPIN_LIMIT
+#define DIP_SPIN_LIMIT (1u << 24)
+#endif
+constexpr uint32_t kSpinLimit = DIP_SPIN_LIMIT;
 constexpr unsigned kErrTimeout = 1u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -4,11 +4,12 @@
 // gate rows (= candidate channels):
 //
 //   workers    phase A  gate GEMV + SiLU over the owned rows -> g; coarse |g|
-//                       histogram; arrive (no wait)
+//                       histogram (no arrival flag: the coordinator checks the
+//                       histogram totals)
 //              spec C   up GEMV of the owned rows with the largest |g| (about
 //                       their expected share of k, nearly always selected),
 //                       started while the selection is computed
-//   CTA 0      waits for every worker's arrival, computes the exact selection
+//   CTA 0      waits until the histograms hold every key, computes the exact selection
 //              (topk_select.cu semantics) over all of g, publishes thresholds
 //              and each worker's tier counts, releases
 //   workers    take the thresholds, list the owned selected rows, write their
@@ -42,7 +43,11 @@ namespace dip {
 #ifdef DIP_TRACE
 __device__ unsigned long long dip_lf_trace[16];
 __device__ unsigned long long dip_lf_cta[160][32];
+__device__ unsigned long long dip_lf_tile[160][64];
 }  // namespace dip
+extern "C" void dip_lf_tile_read(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, dip::dip_lf_tile, 160 * 64 * sizeof(unsigned long long));
+}
 extern "C" void dip_lf_trace_read(unsigned long long* out) {
   cudaMemcpyFromSymbol(out, dip::dip_lf_trace, 16 * sizeof(unsigned long long));
 }
@@ -56,14 +61,21 @@ namespace dip {
 #define LF_CTA(n) \
   do { if (threadIdx.x == 0) { unsigned long long t; \
        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_cta[blockIdx.x][n] = t; } } while (0)
+#define LF_TILE(n) \
+  do { if (threadIdx.x == 0 && (n) < 64) { unsigned long long t; \
+       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_tile[blockIdx.x][n] = t; } } while (0)
 #else
 #define LF_TRACE(n) do { } while (0)
+#define LF_TILE(n) do { } while (0)
 #define LF_CTA(n) do { } while (0)
 #endif
 
 constexpr int kLfWarps = 20;
 constexpr int kLfThreads = kLfWarps * 32;
-constexpr int kLfDepth = 4;
+#ifndef DIP_LF_DEPTH
+#define DIP_LF_DEPTH 3
+#endif
+constexpr int kLfDepth = DIP_LF_DEPTH;  // cp.async ring slots per warp
 constexpr int kLfTilesA = 12;   // max gate tiles (16 rows) per CTA
 constexpr int kLfDnPitch = 144;  // bytes per channel row of a down slot (128 + pad)
 
@@ -111,12 +123,33 @@ struct LfGeom {
   static constexpr int gloc = red + red_words * 4;         // this CTA's g values (bf16)
   static constexpr int lslot = gloc + kLfListMax * 2;      // this CTA's cache slots (CA-DIP)
   static constexpr int misc = lslot + kLfListMax * 4;      // small scalars
-  static constexpr int total = misc + 256;
+  static constexpr int hist = misc + 256;                  // CTA histogram: hash keys,
+  static constexpr int total = hist + 3 * 256 * 4;         // counts, coarse bins
+  static_assert(total <= 227 * 1024, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint16_t ld_cg_u16(const uint16_t* p) {
   unsigned short v;
   asm volatile("ld.global.cg.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_cg_v4u(const uint16_t* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+// Polled words are read with relaxed loads: a weak load (ld.cg) of an
+// unchanged address may be hoisted out of the polling loop.
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_relaxed_v4(const unsigned* p) {  // 16-byte aligned
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ unsigned ld_cg_u32(const unsigned* p) {
@@ -140,6 +173,9 @@ __device__ __forceinline__ void cp_async4_lf(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_commit_lf() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_lf() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(kLfDepth - 1) : "memory");
+}
+__device__ __forceinline__ void cp_wait_lf2() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kLfDepth - 2) : "memory");
 }
 
 // K-slice GEMV step shared by phases A and C: this warp's GW groups of 16
@@ -216,13 +252,16 @@ struct LfSel {
   unsigned long long done;  // final barrier: arrivals of all calls so far (grows by gridDim.x per call)
   unsigned pad_done[30];
   unsigned coarse[256];  // coarse |g| histogram (one bin per bf16 exponent); zero between calls
-  unsigned maxkey;       // largest valid |g| key (atomicMax by the workers); zero between calls
+  unsigned nan_count;    // NaN keys (in no bin): the bins plus this add up to inter once
+                         // every worker's keys are in; zero between calls
   unsigned pad0[31];
   unsigned long long par[4];             // tagged: lo bits, hi bits, totA, filled
   unsigned long long pre[kLfMaxCtas][2];  // tagged, per worker: tier A, tier B counts before it
   unsigned long long cnt[kLfMaxCtas];     // per worker: 1<<63 | tier A << 32 | tier B; zero between calls
   unsigned fine[kTopkHistBins];  // fine |g| histogram (one bin per key); zero between calls
 };
+static_assert(offsetof(LfSel, coarse) % 16 == 0 && offsetof(LfSel, fine) % 16 == 0,
+              "histograms are read in 16-byte pieces");
 __device__ __forceinline__ unsigned lf_tag(unsigned long long done0) {
   return (unsigned)(done0 + 1u) | 0x80000000u;
 }
@@ -267,36 +306,39 @@ __device__ __forceinline__ int lf_row_start(int I, int nwk, int w) {
 }
 
 // CTA 0 coordinates one call in two releases (tagged words of LfSel):
-//   1. once every worker has arrived: the (K+1)-th largest key w from the
+//   1. once the histograms hold every key: the (K+1)-th largest key w from the
 //      coarse and fine histograms, topk_select.cu's 25-step fp32 bisection run
 //      on w, the tier totals -> lo, hi, totA, filled; release 1
 //   2. once every worker has published its tier A / tier B counts: their
 //      exclusive prefix -> pre[]; release 2
-// It clears the coarse histogram, the max word and the count words it read;
-// the workers clear the fine bins they filled.
-__device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* sel, int K, int nb,
+// The workers add their keys with relaxed atomics and no fence or arrival
+// flag: the coarse bins are complete once they and the NaN count add up to I
+// (every count only grows towards its final value), and a coarse bin's fine
+// bins once they add up to its coarse count.  It clears the coarse histogram,
+// the NaN count and the count words it read; the workers clear the fine bins
+// they filled.
+__device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int I, int nb,
                                            unsigned tag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwk = nb - 1;
   __shared__ int s_cnt[2 * kLfMaxCtas];
-  if (tid == 0) {
-    bool ok = false;
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {
-      unsigned c;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(c) : "l"(&bar->count) : "memory");
-      if (c >= (unsigned)nwk) { ok = true; break; }
-    }
-    if (!ok) atomicOr(err, kErrTimeout);
-    __threadfence();
-  }
-  __syncthreads();
-  LF_CTA(13);
   if (warp == 0) {
-    // coarse suffix sums, 8 bins per lane from the top
     int c8[8], loc = 0;
+    bool ok = false;
+    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+      // bins 255 - 8 lane - q, q = 0..7: the 8 words from 248 - 8 lane, reversed
+      const uint4 hi4 = ld_relaxed_v4(sel->coarse + 252 - 8 * lane);
+      const uint4 lo4 = ld_relaxed_v4(sel->coarse + 248 - 8 * lane);
+      c8[0] = (int)hi4.w; c8[1] = (int)hi4.z; c8[2] = (int)hi4.y; c8[3] = (int)hi4.x;
+      c8[4] = (int)lo4.w; c8[5] = (int)lo4.z; c8[6] = (int)lo4.y; c8[7] = (int)lo4.x;
+      loc = 0;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) { c8[q] = (int)ld_cg_u32(sel->coarse + 255 - (lane * 8 + q)); loc += c8[q]; }
-    const unsigned maxkey = ld_cg_u32(&sel->maxkey);
+      for (int q = 0; q < 8; ++q) loc += c8[q];
+      const int nan = lane == 0 ? (int)ld_relaxed_u32(&sel->nan_count) : 0;
+      ok = __reduce_add_sync(0xffffffffu, loc + nan) == I;
+    }
+    if (!ok && lane == 0) atomicOr(err, kErrTimeout);
+    LF_CTA(13);
     int incl = loc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -314,24 +356,51 @@ __device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* s
       for (int qq = 0; qq < 8; ++qq) v = (qq == q) ? suf8[qq] : v;
       return __shfl_sync(0xffffffffu, v, src);
     };
+    auto coarse_at = [&](int bin) -> int {
+      return (bin < 0 || bin >= 256) ? 0 : suffix_at(bin) - suffix_at(bin + 1);
+    };
     const int nvalid = __shfl_sync(0xffffffffu, run, 31);
     const bool has_w = nvalid >= K + 1;
-    int b1 = -1;
+    int b1 = -1, btop = -1;
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
+    for (int q = 0; q < 8; ++q) {
       if (suf8[q] - c8[q] < K + 1 && K + 1 <= suf8[q]) b1 = 255 - (lane * 8 + q);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) b1 = max(b1, __shfl_xor_sync(0xffffffffu, b1, o));
-    // fine bins of b1 - 1, b1, b1 + 1 in one round: lo and hi end within a
-    // key of w, so the tier totals come from these bins too
-    int fb[3][4];
-#pragma unroll
-    for (int d = 0; d < 3; ++d) {
-      const int cb = b1 - 1 + d;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        fb[d][q] = (has_w && cb >= 0 && cb < 256) ? (int)ld_cg_u32(sel->fine + ((cb << 7) | (lane * 4 + q))) : 0;
+      if (c8[q] > 0) btop = max(btop, 255 - (lane * 8 + q));
     }
+    b1 = __reduce_max_sync(0xffffffffu, b1 + 1) - 1;
+    btop = __reduce_max_sync(0xffffffffu, btop + 1) - 1;
+    // fine bins of b1 - 1, b1, b1 + 1 (lo and hi end within a key of w, so
+    // the tier totals come from these too) and of the top coarse bin (the
+    // largest key), loaded together until each adds up to its coarse count
+    int fb[4][4];
+    const int fbin[4] = {b1 - 1, b1, b1 + 1, btop};
+    ok = false;
+    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        const int cb = fbin[d];
+        const bool use = cb >= 0 && cb < 256 && (d == 3 || has_w);
+        const uint4 v = use ? ld_relaxed_v4(sel->fine + ((cb << 7) | (lane * 4)))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        fb[d][0] = (int)v.x; fb[d][1] = (int)v.y; fb[d][2] = (int)v.z; fb[d][3] = (int)v.w;
+      }
+      ok = true;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        const int cb = fbin[d];
+        const bool use = cb >= 0 && cb < 256 && (d == 3 || has_w);
+        const int sum = __reduce_add_sync(0xffffffffu, fb[d][0] + fb[d][1] + fb[d][2] + fb[d][3]);
+        ok = ok && (!use || sum == coarse_at(cb));
+      }
+    }
+    if (!ok && lane == 0) atomicOr(err, kErrTimeout);
+    LF_CTA(15);
+    int kmax = -1;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (btop >= 0 && fb[3][q] > 0) kmax = (btop << 7) | (lane * 4 + q);
+    kmax = __reduce_max_sync(0xffffffffu, kmax + 1) - 1;
+    const unsigned maxkey = kmax < 0 ? 0u : (unsigned)kmax;
     float wv = 0.f;
     if (has_w) {
       const int rank = K + 1 - suffix_at(b1 + 1);
@@ -348,8 +417,7 @@ __device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* s
         runf += fb[1][q];
         if (found < 0 && runf >= rank && runf - fb[1][q] < rank) found = lane * 4 + q;
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(0xffffffffu, found, o));
+      found = __reduce_max_sync(0xffffffffu, found + 1) - 1;
       wv = bf16_bits_to_f32((unsigned)((b1 << 7) | found));
     }
     // topk_select.cu's bisection: hi from the fp32 max of |g|, 25 halvings,
@@ -363,34 +431,46 @@ __device__ __noinline__ void lf_coordinate(GridBar* bar, unsigned* err, LfSel* s
       hi = up ? hi : t;
       t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
     }
+    LF_CTA(20);
     // #keys > tt = #keys >= kmin, kmin the bf16 key just above tt
     auto count_above = [&](float tt) -> int {
       const int kmin = (int)(__float_as_uint(tt) >> 16) + 1;
       if (kmin > 0x7F80) return 0;
       const int cb = kmin >> 7, f0 = kmin & 127, d = cb - (b1 - 1);
-      const bool held = has_w && d >= 0 && d < 3;
+      int fv[4];
+      if (has_w && d >= 0 && d < 3) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) fv[q] = d == 0 ? fb[0][q] : d == 1 ? fb[1][q] : fb[2][q];
+      } else if (cb == btop) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) fv[q] = fb[3][q];
+      } else {  // rare: a bin not loaded above, read until complete
+        const int want = coarse_at(cb);
+        bool okb = false;
+        for (uint32_t it = 0; it < kSpinLimit && !okb; ++it) {
+          const uint4 v = ld_relaxed_v4(sel->fine + ((cb << 7) | (lane * 4)));
+          fv[0] = (int)v.x; fv[1] = (int)v.y; fv[2] = (int)v.z; fv[3] = (int)v.w;
+          okb = __reduce_add_sync(0xffffffffu, fv[0] + fv[1] + fv[2] + fv[3]) == want;
+        }
+        if (!okb && lane == 0) atomicOr(err, kErrTimeout);
+      }
       int part = 0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int f = lane * 4 + q;
-        if (f >= f0) part += held ? (d == 0 ? fb[0][q] : d == 1 ? fb[1][q] : fb[2][q])
-                                  : (int)ld_cg_u32(sel->fine + ((cb << 7) | f));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      return part + suffix_at(cb + 1);
+      for (int q = 0; q < 4; ++q)
+        if (lane * 4 + q >= f0) part += fv[q];
+      return __reduce_add_sync(0xffffffffu, part) + suffix_at(cb + 1);
     };
-    const int totA = count_above(hi), above_lo = count_above(lo);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) sel->coarse[255 - (lane * 8 + q)] = 0u;
+    const int totA = count_above(hi);
+    LF_CTA(23);
+    const int above_lo = count_above(lo);
+    // all keys are in: clear the coarse bins for the next call
+    *reinterpret_cast<uint4*>(sel->coarse + 4 * lane) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(sel->coarse + 128 + 4 * lane) = make_uint4(0u, 0u, 0u, 0u);
+    if (lane == 0) sel->nan_count = 0u;
     if (lane < 4) {  // release 1
       const unsigned v = lane == 0 ? __float_as_uint(lo) : lane == 1 ? __float_as_uint(hi)
                        : lane == 2 ? (unsigned)totA : (unsigned)min(K, above_lo);
       sel->par[lane] = lf_tagged(tag, v);
-    }
-    if (lane == 0) {
-      sel->maxkey = 0u;
-      atomicExch(&bar->count, 0u);  // every worker has arrived
     }
   }
   LF_CTA(14);
@@ -455,7 +535,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
 
   if (b == 0) {
     pdl_wait();
-    lf_coordinate(a.bar, a.err, sel, K, nb, lf_tag(ld_cg_u64(&sel->done)));
+    lf_coordinate(a.err, sel, K, I, nb, lf_tag(ld_cg_u64(&sel->done)));
   } else {
   uint8_t* ring = smem + warp * kLfDepth * Geo::slot;
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Geo::xs);
@@ -482,21 +562,45 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
     cp_commit_lf();
   };
-#pragma unroll
-  for (int i = 0; i < kLfDepth - 1; ++i) issue_a(i);
+  // Only the first tile goes out ahead of the layer input: the input loads
+  // queue behind every line this SM has requested, so the other tiles are
+  // requested right after them.
+  issue_a(0);
   LF_TRACE(0);
   pdl_wait();
   if (tid == 0) s_tag = lf_tag(ld_cg_u64(&sel->done));
   LF_TRACE(1);
 
-  // Layer input: x, or RMSNorm(x + resid); staged in the B-fragment order.
+  // Layer input: x, or RMSNorm(x + resid); one 16-byte word (8 values) per
+  // thread (H / 8 <= kLfThreads, checked on the host), staged in the
+  // B-fragment order.
   {
-    float ssq = 0.f;
+    const int nwords = H / 8;
+    const bool mine = tid < nwords;
+    uint4 xw = make_uint4(0u, 0u, 0u, 0u), rw = make_uint4(0u, 0u, 0u, 0u);
+    if (mine) {
+      xw = ld_cg_v4u(a.x + tid * 8);
+      if (a.resid) rw = ld_cg_v4u(a.resid + tid * 8);
+    }
+#pragma unroll
+    for (int i = 1; i < kLfDepth - 1; ++i) issue_a(i);
+    const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w}, ra[4] = {rw.x, rw.y, rw.z, rw.w};
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] = bf16_bits_to_f32(xa[q] & 0xFFFFu);
+      v[2 * q + 1] = bf16_bits_to_f32(xa[q] >> 16);
+    }
+    float inv = 1.f;
     if (a.resid) {
-      for (int e = tid; e < H; e += kLfThreads) {
-        const float v = bf16_bits_to_f32(ld_cg_u16(a.x + e)) + bf16_bits_to_f32(ld_cg_u16(a.resid + e));
-        ssq = fmaf(v, v, ssq);
+      float ssq = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[2 * q] += bf16_bits_to_f32(ra[q] & 0xFFFFu);
+        v[2 * q + 1] += bf16_bits_to_f32(ra[q] >> 16);
       }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ssq = fmaf(v[e], v[e], ssq);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
       if (lane == 0) misc[warp] = ssq;
@@ -507,46 +611,33 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         misc[32] = rsqrtf(t / (float)H + a.eps);
       }
       __syncthreads();
+      inv = misc[32];
     }
-    const float inv = a.resid ? misc[32] : 1.f;
-    const int nwords = H / 8;
-    for (int wi = tid; wi < ((nwords + kLfThreads - 1) / kLfThreads) * kLfThreads;
-         wi += kLfThreads) {
-      float part = 0.f;
-      if (wi < nwords) {
-        uint32_t v4[4];
+    float part = 0.f;
+    if (mine) {
+      uint32_t v4[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t lo = ld_cg_u16(a.x + wi * 8 + 2 * q), hi = ld_cg_u16(a.x + wi * 8 + 2 * q + 1);
-          uint32_t pr = lo | (hi << 16);
-          if (a.resid) {
-            const uint32_t rl = ld_cg_u16(a.resid + wi * 8 + 2 * q);
-            const uint32_t rh = ld_cg_u16(a.resid + wi * 8 + 2 * q + 1);
-            const float fl = (bf16_bits_to_f32(lo) + bf16_bits_to_f32(rl)) * inv;
-            const float fh = (bf16_bits_to_f32(hi) + bf16_bits_to_f32(rh)) * inv;
-            pr = (uint32_t)f32_to_bf16_bits(fl) | ((uint32_t)f32_to_bf16_bits(fh) << 16);
-          }
-          v4[q] = pr;
-        }
-        if (a.x_used && b == 1)
-          *reinterpret_cast<uint4*>(a.x_used + wi * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
-        uint4 o;
-        o.x = __byte_perm(v4[0], v4[2], 0x5410);
-        o.y = __byte_perm(v4[0], v4[2], 0x7632);
-        o.z = __byte_perm(v4[1], v4[3], 0x5410);
-        o.w = __byte_perm(v4[1], v4[3], 0x7632);
-        const int grp = wi >> 4, t = (wi >> 2) & 3, w = wi & 3;
-        *reinterpret_cast<uint4*>(xs + grp * 72 + t * 16 + (t >> 1) * 4 + 4 * w) = o;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          part += bf16_bits_to_f32(v4[q] & 0xFFFF) + bf16_bits_to_f32(v4[q] >> 16);
+      for (int q = 0; q < 4; ++q) {
+        v4[q] = a.resid ? ((uint32_t)f32_to_bf16_bits(v[2 * q] * inv) |
+                           ((uint32_t)f32_to_bf16_bits(v[2 * q + 1] * inv) << 16))
+                        : xa[q];
+        part += bf16_bits_to_f32(v4[q] & 0xFFFF) + bf16_bits_to_f32(v4[q] >> 16);
       }
-      part += __shfl_xor_sync(0xffffffffu, part, 8);
-      part += __shfl_xor_sync(0xffffffffu, part, 4);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      if ((lane & 15) == 0 && wi < nwords) gsum[wi >> 4] = part;
+      if (a.x_used && b == 1)
+        *reinterpret_cast<uint4*>(a.x_used + tid * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
+      uint4 o;
+      o.x = __byte_perm(v4[0], v4[2], 0x5410);
+      o.y = __byte_perm(v4[0], v4[2], 0x7632);
+      o.z = __byte_perm(v4[1], v4[3], 0x5410);
+      o.w = __byte_perm(v4[1], v4[3], 0x7632);
+      const int grp = tid >> 4, t = (tid >> 2) & 3, w = tid & 3;
+      *reinterpret_cast<uint4*>(xs + grp * 72 + t * 16 + (t >> 1) * 4 + 4 * w) = o;
     }
+    part += __shfl_xor_sync(0xffffffffu, part, 8);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    if ((lane & 15) == 0 && mine) gsum[tid >> 4] = part;
   }
   __syncthreads();
   LF_TRACE(2);
@@ -568,6 +659,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     issue_a(i + kLfDepth - 1);
     cp_wait_lf();
     __syncwarp();
+    LF_TILE(i);
     if (i == 0) LF_CTA(19);
     float pa, pb;
     lf_tile_dot<GW>(ring + (i % kLfDepth) * Geo::slot, xf, bias, lane, sc_sel, pa, pb);
@@ -596,77 +688,92 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     const int t = tid - (kLfThreads - 16 * kLfTilesA);
     if (CA && t >= 0 && t < na) lslot_w[t] = (int)a.id2slot[ra0 + t];
   }
+  unsigned* hkey = reinterpret_cast<unsigned*>(smem + Geo::hist);  // [256] hash slots: key
+  unsigned* hcnt = hkey + 256;                                      // [256] its count
+  unsigned* hcrs = hcnt + 256;                                      // [256] coarse bins
+  __shared__ unsigned s_nnan;
+  for (int i = tid; i < 256; i += kLfThreads) { hkey[i] = 0xFFFFFFFFu; hcnt[i] = 0u; hcrs[i] = 0u; }
+  if (tid == 0) s_nnan = 0u;
   __syncthreads();
-  // |g| histograms, aggregated over the CTA first in shared memory (the ring,
-  // idle now): SiLU's minimum piles ~1/8 of all values into two or three fine
-  // bins and a handful of coarse bins (exponents) take nearly every value, so
-  // per-row global atomics would serialise.  The first row to reach a bin
-  // adds the bin's total.  Plus the largest key (one atomicMax per CTA).
-  {
-    unsigned* sfine = reinterpret_cast<unsigned*>(smem);   // [kTopkHistBins]
-    unsigned* scoarse = sfine + kTopkHistBins;              // [256]
-    __shared__ unsigned s_kmax;
-    const unsigned kk = tid < na ? (gloc[tid] & 0x7FFFu) : 0xFFFFu;
-    const bool valid = kk <= 0x7F80u;
-    if (valid) sfine[kk] = 0u;
-    for (int i = tid; i < 256; i += kLfThreads) scoarse[i] = 0u;
-    if (tid == 0) s_kmax = 0u;
-    __syncthreads();
-    bool lead_f = false, lead_c = false;
-    if (valid) {
-      lead_f = atomicAdd(&sfine[kk], 1u) == 0u;
-      lead_c = atomicAdd(&scoarse[kk >> 7], 1u) == 0u;
-      atomicMax(&s_kmax, kk);
-    }
-    __syncthreads();
-    if (lead_f) atomicAdd(&sel->fine[kk], sfine[kk]);
-    if (lead_c) atomicAdd(&sel->coarse[kk >> 7], scoarse[kk >> 7]);
-    if (tid == 0 && s_kmax) atomicMax(&sel->maxkey, s_kmax);
-  }
-  // arrive (no wait: the coordinator releases the selection later)
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    atomicAdd(&a.bar->count, 1u);
-  }
-  LF_TRACE(4);
-  LF_CTA(2);
-
   // ------------------------------------------------------------ speculation
   // This CTA's nts*16 rows with the largest |g| (about its expected share of
   // k, so nearly all of them end up selected): their up projection starts now,
-  // while the coordinator computes the exact selection.  T = the (nts*16)-th
-  // largest key by a 15-step radix select over the block's keys.
+  // while the coordinator computes the exact selection.  Warp 0 finds T, the
+  // (nts*16)-th largest key, by a 15-step radix select and lists the rows
+  // (keys > T, then keys == T while places remain, each in row order).
   int* crow = reinterpret_cast<int*>(smem + Geo::lists);  // C list: spec rows, then rest rows
   int* drow = crow + kLfListMax;         // D list: selected channels
   int* dsrc = drow + kLfListMax;         // D entry -> C list position
   float* dh = reinterpret_cast<float*>(dsrc + kLfListMax);  // D entry: g, then h
   int* cpos = reinterpret_cast<int*>(dh + kLfListMax);      // local row -> C position or -1
   __shared__ int2 warp_tot[33];
-  for (int r = tid; r < na; r += kLfThreads) cpos[r] = -1;
+  __shared__ int s_nts;
   const unsigned my_key = tid < na ? (gloc[tid] & 0x7FFFu) : 0xFFFFu;
   const bool my_valid = my_key <= 0x7F80u;
-  const int nvalid_loc = __syncthreads_count(my_valid);
-  const int nts = min(na * K / I / 16, nvalid_loc / 16);  // na * K < 2^31 (host check)
-  if (nts > 0) {
-    const int nspec = nts * 16;
-    unsigned T = 0;
-    for (int bit = 14; bit >= 0; --bit) {
-      const unsigned cand = T | (1u << bit);
-      if (__syncthreads_count(my_valid && my_key >= cand) >= nspec) T = cand;
+  if (warp == 0) {
+    constexpr int kPer = (16 * kLfTilesA + 31) / 32;  // rows per lane
+    unsigned key[kPer];
+    int nv = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int r = q * 32 + lane;
+      key[q] = r < na ? (gloc[r] & 0x7FFFu) : 0xFFFFu;
+      if (key[q] > 0x7F80u) key[q] = 0xFFFFu;  // NaN: never speculated
+      nv += key[q] != 0xFFFFu;
+      if (r < na) cpos[r] = -1;
     }
-    // keys > T all fit; keys == T by index while places remain
-    int2 tot;
-    const int2 off = block_excl_scan2(my_valid && my_key > T, my_valid && my_key == T, warp_tot, tot);
-    int pos = -1;
-    if (my_valid && my_key > T) pos = off.x;
-    if (my_valid && my_key == T && tot.x + off.y < nspec) pos = tot.x + off.y;
-    if (pos >= 0) {
-      crow[pos] = ra0 + tid;
-      cpos[tid] = pos;
+    nv = __reduce_add_sync(0xffffffffu, nv);
+    const int nts_w = min(na * K / I / 16, nv / 16);  // na * K < 2^31 (host check)
+    if (nts_w > 0) {
+      const int nspec = nts_w * 16;
+      unsigned T = 0;
+      for (int bit = 14; bit >= 0; --bit) {
+        const unsigned cand = T | (1u << bit);
+        int c = 0;
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) c += key[q] != 0xFFFFu && key[q] >= cand;
+        if (__reduce_add_sync(0xffffffffu, c) >= nspec) T = cand;
+      }
+      const unsigned lt = (1u << lane) - 1u;
+      int pos = 0;
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {  // keys > T
+        const bool gt = key[q] != 0xFFFFu && key[q] > T;
+        const unsigned m = __ballot_sync(0xffffffffu, gt);
+        if (gt) { crow[pos + __popc(m & lt)] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = pos + __popc(m & lt); }
+        pos += __popc(m);
+      }
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {  // keys == T while places remain
+        const bool eq = key[q] == T;
+        const unsigned m = __ballot_sync(0xffffffffu, eq);
+        const int p = pos + __popc(m & lt);
+        if (eq && p < nspec) { crow[p] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = p; }
+        pos += __popc(m);
+      }
+    }
+    if (lane == 0) s_nts = max(nts_w, 0);
+  } else if ((warp - 1) * 32 < na) {
+    // |g| histograms of this CTA's keys: equal keys are merged in a shared
+    // memory hash table first (SiLU's minimum piles ~1/8 of all values onto
+    // two or three keys; per-row global atomics on them would serialise).
+    const int r = (warp - 1) * 32 + lane;
+    if (r < na) {
+      const unsigned kk = gloc[r] & 0x7FFFu;
+      if (kk <= 0x7F80u) {
+        unsigned h = (kk * 0x9E3779B1u) >> 24;
+        for (int p = 0; p < 256; ++p, h = (h + 1) & 255u) {
+          const unsigned old = atomicCAS(&hkey[h], 0xFFFFFFFFu, kk);
+          if (old == 0xFFFFFFFFu || old == kk) { atomicAdd(&hcnt[h], 1u); break; }
+        }
+        atomicAdd(&hcrs[kk >> 7], 1u);
+      } else {
+        atomicAdd(&s_nnan, 1u);
+      }
     }
   }
   __syncthreads();
+  const int nts = s_nts;
   LF_CTA(3);
 
   // ------------------------------------------------------------ phases C + D
@@ -677,7 +784,26 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   __shared__ int s_par[4];
   __shared__ int s_n[2];
   int nC = nts, nD = 0, nDA = 0;
-  bool have1 = false, have2 = false;
+  bool have1 = false, have2 = false, c_done = false;
+  // h = bf16(g * bf16(u)) for down list entries [r0, r1) once their up sums
+  // are complete (entries hold g until then)
+  auto make_h = [&](int r0, int r1) {
+    const int pad_row = s_n[0];
+    const float mult = (float)s_n[1];
+    for (int r = r0 + tid; r < r1; r += kLfThreads) {
+      const int src = dsrc[r];
+      float h = 0.f;
+      if (src >= 0) {
+        const int ti = src >> 4, row = src & 15;
+        float v = 0.f;
+        for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
+        h = round_bf16(dh[r] * round_bf16(v));
+        if (r == pad_row) h *= mult;
+      }
+      dh[r] = h;
+    }
+    __syncthreads();
+  };
   // Row sources: channel ch (one of this CTA's rows) reads its up / down row
   // from the resident cache when it has a slot there, else from the full
   // matrices.
@@ -728,7 +854,8 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // Release 1: the thresholds.  Publish this CTA's tier counts, clear the fine
   // bins it filled, queue the up rows of its tier A rows and tie candidates
   // not speculated on, and list its tier A rows for the down projection.
-  auto need1 = [&]() {
+  auto poll1 = [&]() {
+    LF_CTA(6);
     if (tid == 0) {
       const unsigned tag = s_tag;
       unsigned long long p[4];
@@ -746,17 +873,20 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       s_par[1] = (int)(unsigned)p[3];
     }
     __syncthreads();
+  };
+  auto apply1 = [&]() {
     LF_CTA(8);
     const float lo = s_lohi[0], hi = s_lohi[1];
     isA = kv > hi;
     isB = kv > lo && kv <= hi;
     offAB = block_excl_scan2(isA, isB, warp_tot, totAB);
+    if (my_valid) sel->fine[my_key] = 0u;  // the coordinator has read the fine bins
     if (tid == 0) {
       const unsigned long long word =
           (1ull << 63) | ((unsigned long long)totAB.x << 32) | (unsigned)totAB.y;
-      asm volatile("st.release.gpu.global.u64 [%0], %1;\n" ::"l"(sel->cnt + b), "l"(word) : "memory");
+      // the word is its own payload: a relaxed store suffices
+      asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(sel->cnt + b), "l"(word) : "memory");
     }
-    if (my_valid) sel->fine[my_key] = 0u;
     // the owner of row 0 may need channel 0 for the index padding
     const bool pad_maybe = b == 1 && s_par[1] < K;
     const bool restr = tid < na && (isA || isB || (pad_maybe && tid == 0)) && cpos[tid] < 0;
@@ -776,11 +906,14 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
     nC = nts + ntr;
     nDA = totAB.x;
+    nD = nDA / 16;  // the full tier A tiles need no release 2
+    if (tid == 0) s_n[0] = -1;
     __syncthreads();
   };
   // Release 2: this CTA's prefix counts.  Write its part of idx, append the
   // selected tie rows and the padding entry to the down list.
-  auto need2 = [&]() {
+  auto poll2 = [&]() {
+    LF_CTA(7);
     if (tid == 0) {
       const unsigned tag = s_tag;
       unsigned long long p0 = 0, p1 = 0;
@@ -795,6 +928,8 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       s_par[3] = (int)(unsigned)p1;
     }
     __syncthreads();
+  };
+  auto apply2 = [&]() {
     LF_CTA(9);
     const int totA = s_par[0], filled = s_par[1], selB = filled - totA;
     const int preA = s_par[2], preB = s_par[3];
@@ -832,18 +967,38 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
     nD = ntd;
     __syncthreads();
+    if (c_done) make_h(nDA, nD * 16);
   };
+  // Release 1 before the first rest up tile; release 2 before the first down
+  // tile that is not a full tile of tier A rows.
+  // (blocking poll only when the stream reaches that point first)
   auto need = [&](int j) {  // before issuing stream index j
-    if (!have1 && j >= nts) { need1(); have1 = true; }
-    if (have1 && !have2 && j >= nC) { need2(); have2 = true; }
+    if (!have1 && j >= nts) { poll1(); apply1(); have1 = true; }
+    if (have1 && !have2 && j >= nC + nD) { poll2(); apply2(); have2 = true; }
   };
+  // Per stream index j: wait for tile j, issue tile j + kLfDepth - 1 (into
+  // the slot tile j - 1 used), compute tile j.
+  // This CTA's part of the global histograms: one relaxed atomic per distinct
+  // key and coarse bin, no fence and no arrival flag (the coordinator checks
+  // the totals), then the stream goes on at once.
+  if (tid < 256) {
+    const unsigned kk = hkey[tid];
+    if (kk != 0xFFFFFFFFu) atomicAdd(&sel->fine[kk], hcnt[tid]);
+  } else if (tid < 512) {
+    const unsigned c = hcrs[tid - 256];
+    if (c) atomicAdd(&sel->coarse[tid - 256], c);
+  } else if (tid == 512 && s_nnan) {
+    atomicAdd(&sel->nan_count, s_nnan);
+  }
+  LF_CTA(2);
 #pragma unroll 1
   for (int j = 0; j < kLfDepth - 1; ++j) { need(j); issue(j); }
   for (int j = 0; j < nC; ++j) {
+    cp_wait_lf2();
+    __syncwarp();
+    LF_TILE(16 + j);
     need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
-    cp_wait_lf();
-    __syncwarp();
     float pa, pb;
     lf_tile_dot<GW>(ring + (j % kLfDepth) * Geo::slot, xf, bias, lane, sc_sel, pa, pb);
     if (tq == 0) {
@@ -852,25 +1007,10 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
     __syncwarp();
   }
-  // h = bf16(g * bf16(u)) for the down list, while its first tiles are in flight
+  // h for the down list known so far, while its first tiles are in flight
   __syncthreads();
-  {
-    const int pad_row = s_n[0];
-    const float mult = (float)s_n[1];
-    for (int r = tid; r < nD * 16; r += kLfThreads) {
-      const int src = dsrc[r];
-      float h = 0.f;
-      if (src >= 0) {
-        const int ti = src >> 4, row = src & 15;
-        float v = 0.f;
-        for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
-        h = round_bf16(dh[r] * round_bf16(v));
-        if (r == pad_row) h *= mult;
-      }
-      dh[r] = h;
-    }
-  }
-  __syncthreads();
+  make_h(0, have2 ? nD * 16 : nDA);
+  c_done = true;
   LF_TRACE(7);
   LF_CTA(10);
   float acc[GW][8][4];
@@ -883,10 +1023,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   for (int u = 0; u < GW; ++u) colsum[u] = 0.f;
   const int tpair = lane & 7, twhich = (lane >> 3) & 1;
   for (int j = nC; j < nC + nD; ++j) {
+    cp_wait_lf2();
+    __syncwarp();
+    LF_TILE(16 + j);
     need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
-    cp_wait_lf();
-    __syncwarp();
     if (j == nC) LF_CTA(17);
     const uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
     const int i = j - nC;
@@ -1074,7 +1215,7 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
   int gw = 0;
   if (H % kGroup == 0 && G == kLfWarps * 1) gw = 1;
   if (H % kGroup == 0 && G == kLfWarps * 2) gw = 2;
-  if (!gw) return DIP_ERR_UNSUPPORTED;
+  if (!gw || I % 8 != 0) return DIP_ERR_UNSUPPORTED;
   // per-worker limits (CTA 0 coordinates): gate rows <= 16*kLfTilesA - 1
   // (C list: rows plus one padding entry, in at most kLfTilesA + 1 tiles)
   if (nb < 2 || (I + nb - 2) / (nb - 1) > 16 * kLfTilesA - 1 || I * (int64_t)nb >= (int64_t(1) << 31) ||
@@ -1084,6 +1225,7 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
   if (workspace_bytes < dip_mlp_fused_workspace_bytes(H, I, k)) return DIP_ERR_WORKSPACE;
   const uintptr_t al = reinterpret_cast<uintptr_t>(L->gate_qw) | reinterpret_cast<uintptr_t>(L->up_qw) |
                        reinterpret_cast<uintptr_t>(L->down_t_qw) | reinterpret_cast<uintptr_t>(x) |
+                       reinterpret_cast<uintptr_t>(resid) | reinterpret_cast<uintptr_t>(x_used) |
                        reinterpret_cast<uintptr_t>(g_out) | reinterpret_cast<uintptr_t>(workspace);
   if (al & 15) return DIP_ERR_ARG;
   uint8_t* ws = static_cast<uint8_t*>(workspace);

@@ -223,8 +223,9 @@ DIP_API int dip_mlp_decode(const dip_layer_t* layer, const dip_bf16* x, int64_t 
  * the inter-layer step of the synthetic stack; x_used (optional) receives the
  * input used.  The workspace (dip_mlp_fused_workspace_bytes) must be ZERO
  * before its first use and is left reusable.  Weights, x, g_out and the
- * workspace must be 16-byte aligned (DIP_ERR_ARG otherwise).  Requires
- * hidden = 2560 or 5120 (20 warps x 1 or 2 quantisation groups) and at most
+ * workspace, and resid / x_used when given, must be 16-byte aligned
+ * (DIP_ERR_ARG otherwise).  Requires
+ * hidden = 2560 or 5120 (20 warps x 1 or 2 quantisation groups), inter a multiple of 8 and at most
  * 16*12-1 gate rows per SM; otherwise DIP_ERR_UNSUPPORTED. */
 DIP_API size_t dip_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k);
 DIP_API int dip_mlp_decode_fused(const dip_layer_t* layer, const dip_bf16* x,
