@@ -344,8 +344,9 @@ def _free_port():
 
 def run_config3(args):
     """Config 3: B independent tokens per step through the 64-layer stack
-    (per-token DIP; the gate GEMV of up to 8 tokens shares one weight pass).
-    `value` is tokens per second of the whole batch."""
+    (per-token DIP selection; `--path tc` (default) streams every weight once
+    for the batch through the tcgen05 GEMMs, `--path gather` gathers each
+    token's rows).  `value` is tokens per second of the whole batch."""
     import dip_b200  # noqa: F401
     from dip_b200.stack import StackConfig, layer_weight_bytes
     from dip_b200.batch import BatchedDipStack
@@ -353,7 +354,8 @@ def run_config3(args):
     torch.cuda.set_device(dev)
     B = args.batch
     cfg = StackConfig(n_layers=args.layers, seed=0)
-    stack = BatchedDipStack(cfg, B, dev)
+    stack = BatchedDipStack(cfg, B, dev, path=args.path if args.path in ("tc", "gather") else "auto")
+    path = stack.path
     T = args.warmup + args.steps
     gen = torch.Generator().manual_seed(3000)
     x0 = torch.randn(T, B, cfg.hidden, generator=gen).to(torch.bfloat16).to(dev)
@@ -374,7 +376,13 @@ def run_config3(args):
     ms = e0.elapsed_time(e1) / args.steps
     nb = layer_weight_bytes(cfg)
     passes = (B + 7) // 8
-    layer_bytes = passes * nb["gate"] + B * (nb["up"] + nb["down"])
+    if path == "tc":  # every row of the three matrices once per step
+        layer_bytes = nb["gate"] * 3
+        # permute + gate, top-k, counts, permute + up, down + reduce, RMSNorm
+        launches = 9
+    else:
+        layer_bytes = passes * nb["gate"] + B * (nb["up"] + nb["down"])
+        launches = passes + 1 + 2 * B + 1
     layer_us = ms * 1e3 / cfg.n_layers
     peak, peak_kind = _peaks()
     print(json.dumps({
@@ -383,11 +391,11 @@ def run_config3(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
         "config": {"workload": f"config3: 64-layer stack, batch {B} independent tokens",
-                   "batch": B, "layers": cfg.n_layers, "k": cfg.k},
+                   "batch": B, "layers": cfg.n_layers, "k": cfg.k, "path": path},
         "us_per_layer": layer_us, "us_per_token_layer": layer_us / B,
         "layer_bytes": layer_bytes, "layer_hbm_gbs": layer_bytes / (layer_us * 1e-6) / 1e9,
         "layer_hbm_frac": layer_bytes / (layer_us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
-        "gpu_launches": args.steps * cfg.n_layers * (passes + 1 + 2 * B + 1),
+        "gpu_launches": args.steps * cfg.n_layers * launches,
         "clocks": clk}), flush=True)
 
 
@@ -551,8 +559,9 @@ def main():
                     help="config 4: shard every layer along I over the torchrun ranks")
     ap.add_argument("--single-layer", type=int, default=0, metavar="N",
                     help="profiling aid: N launches of one config-1 fused layer, then exit")
-    ap.add_argument("--path", default="fused", choices=["fused", "chain"],
-                    help="fused: one persistent kernel per layer; chain: separate launches")
+    ap.add_argument("--path", default="fused", choices=["fused", "chain", "tc", "gather"],
+                    help="config 1: fused (one persistent kernel per layer) or chain (separate "
+                         "launches); config 3: tc (default, dense tcgen05 GEMMs) or gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.single_layer:

@@ -358,6 +358,72 @@ Tensor residual_rmsnorm(const Tensor& y_in, const Tensor& r_in, double eps) {
   return out;
 }
 
+// batched decode / dense forward on tcgen05: x [B, in] -> [B, rows]
+Tensor gemm_tc(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, int64_t epilogue,
+               const c10::optional<Tensor>& g_in, const c10::optional<Tensor>& cnt_in) {
+  check_packed(qweight, scales, "gemm_tc");
+  Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_dtype(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.dim() == 2 && x.size(1) == qweight.size(1) * 2, "gemm_tc: x must be [B, in]");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty({x.size(0), qweight.size(0)}, x.options());
+  if (x.size(0) == 0) return out;
+  Tensor g, cnt;
+  const uint16_t* gp = nullptr;
+  const uint32_t* cp = nullptr;
+  if (epilogue == 2) {
+    TORCH_CHECK(g_in.has_value() && cnt_in.has_value(), "gemm_tc: epilogue 2 needs g and cnt");
+    g = g_in->contiguous();
+    cnt = cnt_in->contiguous();
+    check_dtype(g, at::kBFloat16, "g");
+    check_dtype(cnt, at::kInt, "cnt");
+    TORCH_CHECK(g.sizes() == out.sizes() && cnt.sizes() == out.sizes(), "gemm_tc: g / cnt must be [B, rows]");
+    gp = bf(g);
+    cp = reinterpret_cast<const uint32_t*>(cnt.data_ptr<int32_t>());
+  }
+  const size_t nws = dip_int4_gemm_tc_workspace_bytes(x.size(1), x.size(0));
+  Tensor ws = at::empty({(int64_t)nws}, x.options().dtype(at::kByte));
+  check_status(dip_int4_gemm_tc(i8(qweight), bf(scales), bf(x), qweight.size(0), x.size(1), x.size(0),
+                                (int)epilogue, gp, cp, ws.data_ptr(), nws, bfm(out), cur_stream()),
+               "gemm_tc");
+  return out;
+}
+
+// h [B, inter] -> y [B, hidden] over the transposed down weights
+Tensor down_tc(const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& h_in) {
+  check_packed(dt_qw, dt_sc, "down_tc");
+  Tensor h = h_in.contiguous();
+  check_cuda(h, "h");
+  check_dtype(h, at::kBFloat16, "h");
+  TORCH_CHECK(h.dim() == 2 && h.size(1) == dt_qw.size(0), "down_tc: h must be [B, inter]");
+  c10::cuda::CUDAGuard guard(h.device());
+  const int64_t out_f = dt_qw.size(1) * 2, B = h.size(0);
+  Tensor y = at::empty({B, out_f}, h.options());
+  if (B == 0) return y;
+  const size_t nws = dip_int4_down_tc_workspace_bytes(out_f, B);
+  Tensor ws = at::empty({(int64_t)nws}, h.options().dtype(at::kByte));
+  check_status(dip_int4_down_tc(i8(dt_qw), bf(dt_sc), bf(h), dt_qw.size(0), out_f, B, ws.data_ptr(),
+                                nws, bfm(y), cur_stream()),
+               "down_tc");
+  return y;
+}
+
+// idx [B, k] -> cnt [B, inter] (int32 counts)
+Tensor select_count(const Tensor& idx_in, int64_t inter) {
+  Tensor idx = idx_in.contiguous();
+  check_cuda(idx, "idx");
+  check_dtype(idx, at::kInt, "idx");
+  TORCH_CHECK(idx.dim() == 2, "select_count: idx must be [B, k]");
+  c10::cuda::CUDAGuard guard(idx.device());
+  Tensor cnt = at::empty({idx.size(0), inter}, idx.options());
+  if (idx.size(0) == 0) return cnt;
+  check_status(dip_select_count(idx.data_ptr<int32_t>(), idx.size(0), idx.size(1), inter,
+                                reinterpret_cast<uint32_t*>(cnt.data_ptr<int32_t>()), cur_stream()),
+               "select_count");
+  return cnt;
+}
+
 // config 3: x [B, in] -> [B, rows] (gate GEMV with SiLU, or plain)
 Tensor gemv_batched(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, bool silu) {
   check_packed(qweight, scales, "gemv_batched");
@@ -562,6 +628,9 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
   m.def("residual_rmsnorm(Tensor y, Tensor r, float eps) -> Tensor");
   m.def("gemv_batched(Tensor qweight, Tensor scales, Tensor x, bool silu) -> Tensor");
+  m.def("gemm_tc(Tensor qweight, Tensor scales, Tensor x, int epilogue, Tensor? g=None, Tensor? cnt=None) -> Tensor");
+  m.def("down_tc(Tensor down_t_qw, Tensor down_t_sc, Tensor h) -> Tensor");
+  m.def("select_count(Tensor idx, int inter) -> Tensor");
   m.def("shard_select(Tensor idx, int lo, int hi) -> (Tensor, Tensor)");
   m.def(
       "gather_up_h_count(Tensor up_qw, Tensor up_sc, Tensor x, Tensor g, Tensor idx, "
@@ -589,6 +658,9 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("transpose_down_int4", &transpose_down_int4);
   m.impl("residual_rmsnorm", &residual_rmsnorm);
   m.impl("gemv_batched", &gemv_batched);
+  m.impl("gemm_tc", &gemm_tc);
+  m.impl("down_tc", &down_tc);
+  m.impl("select_count", &select_count);
   m.impl("shard_select", &shard_select);
   m.impl("gather_up_h_count", &gather_up_h_count);
   m.impl("gather_down_partial", &gather_down_partial);

@@ -119,6 +119,18 @@ def _register_fakes_fused():
     def _(qweight, scales, x, silu):
         return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)
 
+    @torch.library.register_fake("dip_b200::gemm_tc")
+    def _(qweight, scales, x, epilogue, g=None, cnt=None):
+        return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)
+
+    @torch.library.register_fake("dip_b200::down_tc")
+    def _(dt_qw, dt_sc, h):
+        return torch.empty(h.shape[0], dt_qw.shape[1] * 2, dtype=torch.bfloat16, device=h.device)
+
+    @torch.library.register_fake("dip_b200::select_count")
+    def _(idx, inter):
+        return torch.empty(idx.shape[0], inter, dtype=torch.int32, device=idx.device)
+
 
 def header_symbols() -> list[str]:
     """Every function the public header declares (DIP_API ...)."""

@@ -256,6 +256,46 @@ DIP_API int dip_mlp_decode_fused_ca(const dip_layer_t* layer, const dip_ca_cache
                                     dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
                                     dip_stream_t stream);
 
+/* ---- batched decode and dense forward on tcgen05 tensor cores ------------------
+ * The reference decode path is batch-1 (dip_stream_predispatch.py:170, :182); a
+ * batch of B tokens is B independent DIP decodes.  These entry points compute
+ * them with dense int4 x bf16 GEMMs on the 5th-generation tensor cores
+ * (M = 128 weight rows per tile, N = B padded to 16/32/64/128, fp32
+ * accumulators in TMEM), every weight dequantised to bf16(q * s) as
+ * dequantize() (qlinear.py:28-64) does.
+ *
+ * dip_int4_gemm_tc: out[b][r] = epi(sum_k W[r][k] x[b][k]), W in the layout of
+ * QuantLinear (qweight [rows, in/2], scales [rows, in/128]; replaces
+ * QuantLinear.forward's F.linear(x, dequantize(...)), qlinear.py:86-88, for
+ * 1 <= batch <= 128).  epilogue 0: bf16(acc); 1: bf16(silu(bf16(acc))) (the
+ * gate, dip_stream_predispatch.py:182); 2: the DIP up product
+ * h = bf16(g * bf16(acc)) * sel_count (dip_stream_predispatch.py:199-201 with
+ * the token's selected channels, sel_count[b][r] = times r is in its index
+ * list; 0 = not selected, h = 0), g and sel_count [batch, rows].  in_features
+ * a multiple of 256; qweight, x and the workspace (a reordered copy of x,
+ * dip_int4_gemm_tc_workspace_bytes) 16-byte aligned, scales 4-byte aligned. */
+DIP_API size_t dip_int4_gemm_tc_workspace_bytes(int64_t in_features, int64_t batch);
+DIP_API int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
+                             int64_t rows, int64_t in_features, int64_t batch, int epilogue,
+                             const dip_bf16* g, const uint32_t* sel_count, void* workspace,
+                             size_t workspace_bytes, dip_bf16* out, dip_stream_t stream);
+/* Dense down projection of a batch over the transposed down weights
+ * (down_t [inter, out/2] + scales [inter, out/128] of _transpose_down_to_int4,
+ * dip_stream_predispatch.py:100-120): y[b] = bf16(sum_c h[b][c] W_down_t[c]),
+ * h [batch, inter] (zero for unselected channels; replaces the per-token
+ * int4_gather_down, int4_gather_down.cu:41-95).  Channels are split over the
+ * SMs; the fp32 partials (workspace, dip_int4_down_tc_workspace_bytes) are
+ * summed in a fixed order.  out a multiple of 256, inter of 64. */
+DIP_API size_t dip_int4_down_tc_workspace_bytes(int64_t out_features, int64_t batch);
+DIP_API int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
+                             int64_t inter, int64_t out_features, int64_t batch, void* workspace,
+                             size_t workspace_bytes, dip_bf16* y, dip_stream_t stream);
+/* cnt[b][c] = how many times channel c occurs in idx[b] (idx [batch, k]), the
+ * selection of each token as dense counts for dip_int4_gemm_tc's epilogue 2
+ * (the reference's index_select over idx, dip_stream_predispatch.py:199-203). */
+DIP_API int dip_select_count(const int32_t* idx, int64_t batch, int64_t k, int64_t inter,
+                             uint32_t* cnt, dip_stream_t stream);
+
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit
  * exact with scripts/quantize.py:32-64. */

@@ -32,7 +32,7 @@ def test_batched_layer_matches_batch1(dip, oracle):
     cfg = StackConfig(n_layers=1, seed=8)
     L = make_layer(cfg, 0, torch.device("cuda", 0))
     x = torch.randn(4, cfg.hidden, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).cuda()
-    y, g, idx = batched_dip_layer(L, x, cfg.k)
+    y, g, idx = batched_dip_layer(L, x, cfg.k, "gather")
     for b in range(4):
         y1, g1, i1 = torch.ops.dip_b200.mlp_decode(L["gate_qw"], L["gate_sc"], L["up_qw"],
                                                    L["up_sc"], L["down_t_qw"], L["down_t_sc"],
@@ -51,3 +51,34 @@ def test_rmsnorm_rows(dip):
     out = torch.ops.dip_b200.residual_rmsnorm(y, r, 1e-6)
     for b in range(5):
         assert torch.equal(out[b], torch.ops.dip_b200.residual_rmsnorm(y[b], r[b], 1e-6))
+
+
+@pytest.mark.parametrize("B", [4, 64])
+def test_batched_layer_tc_matches_reference(dip, oracle, B):
+    """The tcgen05 batched layer per token against the reference's pure-PyTorch
+    DIP math (dequantize + topk + index_select + matmul): g within tolerance of
+    F.silu(F.linear(x, dequantize(W_gate))), idx exactly topk_select of the
+    token's g, y within tolerance of the reference products over that idx."""
+    import torch.nn.functional as F
+    from dip_b200.stack import StackConfig, make_layer
+    from dip_b200.batch import batched_dip_layer
+    cfg = StackConfig(n_layers=1, seed=12)
+    L = make_layer(cfg, 0, torch.device("cuda", 0))
+    x = torch.randn(B, cfg.hidden, generator=torch.Generator().manual_seed(B)).to(torch.bfloat16).cuda()
+    y, g, idx = batched_dip_layer(L, x, cfg.k, "tc")
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    cpu = {n: t.cpu() for n, t in L.items()}
+    wg = oracle.dequantize(cpu["gate_qw"], cpu["gate_sc"])
+    g_ref = F.silu(F.linear(x.cpu(), wg))
+    gc, ic, yc = g.cpu(), idx.cpu(), y.cpu()
+    err = (gc.float() - g_ref.float()).abs()
+    assert bool((err <= 2e-3 + 1e-2 * g_ref.float().abs()).all())
+    for b in (range(B) if B <= 4 else (0, 17, 63)):
+        assert torch.equal(ic[b], oracle.topk_select(gc[b], cfg.k))
+        il = ic[b].long()
+        u = F.linear(x[b:b + 1].cpu(), oracle.dequantize(cpu["up_qw"][il], cpu["up_sc"][il]))[0]
+        h = (gc[b][il].float() * u.float()).to(torch.bfloat16)
+        ref = h.float() @ oracle.dequantize(cpu["down_t_qw"][il], cpu["down_t_sc"][il]).float()
+        e = (yc[b].float() - ref).abs()
+        assert bool((e <= 2e-3 + 1e-2 * ref.abs() + 4e-4 * ref.abs().max()).all()), float(e.max())
