@@ -57,7 +57,8 @@ struct TcArgs {
   const uint16_t* s;  // rows: [R, K/128]; trans: [K, R/128]
   const uint16_t* x;  // [B, K] activations (B operand), row stride K
   int R, K, B;
-  int ksplit;         // K ranges per tile (trans only; 1 otherwise)
+  int ksplit;         // K ranges per tile (their fp32 partials are summed by tc_reduce_kernel)
+  int kgran;          // K steps a range is a multiple of (rows: one raw chunk)
   uint16_t* out;      // [B, R] bf16 (kTcEpiBf16 / Silu / H)
   float* out_f32;     // kTcEpiF32: [ksplit][B][R] partial sums
   const uint16_t* g;  // kTcEpiH: [B, R] gate activations
@@ -207,10 +208,10 @@ struct TcUnit {
   int tile, k0, nsteps;
 };
 __device__ __forceinline__ TcUnit tc_unit(const TcArgs& a, int u) {
-  const int ksteps = a.K / kTcK;
+  const int kunits = a.K / (kTcK * a.kgran);
   const int tile = u / a.ksplit, part = u % a.ksplit;
-  const int s0 = (int)((int64_t)ksteps * part / a.ksplit);
-  const int s1 = (int)((int64_t)ksteps * (part + 1) / a.ksplit);
+  const int s0 = (int)((int64_t)kunits * part / a.ksplit) * a.kgran;
+  const int s1 = (int)((int64_t)kunits * (part + 1) / a.ksplit) * a.kgran;
   return {tile, s0 * kTcK, s1 - s0};
 }
 
@@ -272,21 +273,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
     // l&1, lanes 0-15 the rows' scale words) through a kTcRawC-deep ring; per
     // K step (64) lane l dequantises 16 bytes of row l/2 (K half l&1).
     uint8_t* wring = smem + Sm::raw + warp * kTcRawC * Sm::wslot;
-    const int nck = a.K / kTcChunkK;  // chunks per unit (ksplit == 1)
-    const int nchunks_total = nsteps_total / (kTcChunkK / kTcK);
+    constexpr int kStepsPerChunk = kTcChunkK / kTcK;
+    const int nchunks_total = nsteps_total / kStepsPerChunk;
     int iu = blockIdx.x, ic = 0;
+    TcUnit iun = iu < nunits ? tc_unit(a, iu) : TcUnit{0, 0, 0};
     auto issue_chunk = [&](int gc) {
       if (gc < nchunks_total) {
-        if (ic >= nck) { iu += gridDim.x; ic = 0; }
-        const int row = min(iu / a.ksplit * kTcM + warp * 16 + (lane >> 1), a.R - 1);
+        while (ic >= iun.nsteps / kStepsPerChunk) { iu += gridDim.x; iun = tc_unit(a, iu); ic = 0; }
+        const int cidx = iun.k0 / kTcChunkK + ic;  // chunk of the row
+        const int row = min(iun.tile * kTcM + warp * 16 + (lane >> 1), a.R - 1);
         uint8_t* slot = wring + (gc % kTcRawC) * Sm::wslot;
-        const uint8_t* src = a.w + (size_t)row * (a.K / 2) + (size_t)ic * 128 + (lane & 1) * 64;
+        const uint8_t* src = a.w + (size_t)row * (a.K / 2) + (size_t)cidx * 128 + (lane & 1) * 64;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           cp_async16_zfill(slot + (lane >> 1) * 128 + (lane & 1) * 64 + i * 16, src + i * 16, true);
         if (lane < 16) {
-          const int srow = min(iu / a.ksplit * kTcM + warp * 16 + lane, a.R - 1);
-          cp_async4_tc(slot + 16 * 128 + lane * 4, a.s + (size_t)srow * (a.K / 128) + ic * 2);
+          const int srow = min(iun.tile * kTcM + warp * 16 + lane, a.R - 1);
+          cp_async4_tc(slot + 16 * 128 + lane * 4, a.s + (size_t)srow * (a.K / 128) + cidx * 2);
         }
         ++ic;
       }
@@ -347,6 +350,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
             // (columns past NT are allocated, kCols >= 32)
             tc_ld16(tbase + c0, v);
           }
+          // EPI_H: the block's g and selection counts, loaded together
+          uint16_t gv[16];
+          uint32_t cv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = half * kHalfN + c0 + i;
+            const bool ok = EPI == kTcEpiH && c0 + i < kHalfN && n < a.B && row < a.R;
+            gv[i] = ok ? a.g[(size_t)n * a.R + row] : (uint16_t)0;
+            cv[i] = ok ? a.cnt[(size_t)n * a.R + row] : 0u;
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = half * kHalfN + c0 + i;
@@ -357,9 +370,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
             } else if (EPI == kTcEpiSilu) {
               a.out[o] = f32_to_bf16_bits(silu_f32(round_bf16(v[i])));
             } else if (EPI == kTcEpiH) {
-              const uint32_t c = a.cnt[o];
+              const uint32_t c = cv[i];
               float h = 0.f;
-              if (c) h = round_bf16(bf16_bits_to_f32(a.g[o]) * round_bf16(v[i])) * (float)c;
+              if (c) h = round_bf16(bf16_bits_to_f32(gv[i]) * round_bf16(v[i])) * (float)c;
               a.out[o] = f32_to_bf16_bits(h);
             } else {
               a.out[o] = f32_to_bf16_bits(v[i]);
@@ -467,6 +480,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
             // (columns past NT are allocated, kCols >= 32)
             tc_ld16(tbase + c0, v);
           }
+          // EPI_H: the block's g and selection counts, loaded together
+          uint16_t gv[16];
+          uint32_t cv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = half * kHalfN + c0 + i;
+            const bool ok = EPI == kTcEpiH && c0 + i < kHalfN && n < a.B && row < a.R;
+            gv[i] = ok ? a.g[(size_t)n * a.R + row] : (uint16_t)0;
+            cv[i] = ok ? a.cnt[(size_t)n * a.R + row] : 0u;
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = half * kHalfN + c0 + i;
@@ -477,9 +500,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
             } else if (EPI == kTcEpiSilu) {
               a.out[o] = f32_to_bf16_bits(silu_f32(round_bf16(v[i])));
             } else if (EPI == kTcEpiH) {
-              const uint32_t c = a.cnt[o];
+              const uint32_t c = cv[i];
               float h = 0.f;
-              if (c) h = round_bf16(bf16_bits_to_f32(a.g[o]) * round_bf16(v[i])) * (float)c;
+              if (c) h = round_bf16(bf16_bits_to_f32(gv[i]) * round_bf16(v[i])) * (float)c;
               a.out[o] = f32_to_bf16_bits(h);
             } else {
               a.out[o] = f32_to_bf16_bits(v[i]);
@@ -574,15 +597,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcArgs a) 
   }
 }
 
-// Fixed-order sum of the split-K partials: y[b][r] = bf16(sum_p part[p][b][r]).
-__global__ void tc_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t n,
+// Fixed-order sum of the split-K partials, then the epilogue:
+// y[i] = epi(sum_p part[p][i]) (kTcEpiBf16 / Silu / H as in the GEMM).
+__global__ void tc_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t n, int epi,
+                                 const uint16_t* __restrict__ g, const uint32_t* __restrict__ cnt,
                                  uint16_t* __restrict__ y) {
   pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int p = 0; p < ksplit; ++p) s += part[p * n + i];
-    y[i] = f32_to_bf16_bits(s);
+    float o = s;
+    if (epi == kTcEpiSilu) {
+      o = silu_f32(round_bf16(s));
+    } else if (epi == kTcEpiH) {
+      const uint32_t c = cnt[i];
+      o = c ? round_bf16(bf16_bits_to_f32(g[i]) * round_bf16(s)) * (float)c : 0.f;
+    }
+    y[i] = f32_to_bf16_bits(o);
   }
 }
 
@@ -619,9 +651,26 @@ static int tc_check_rows(const void* w, const void* s, const void* x, int64_t R,
   return DIP_OK;
 }
 
-extern "C" size_t dip_int4_gemm_tc_workspace_bytes(int64_t in_features, int64_t batch) {
-  if (in_features <= 0 || batch <= 0) return 0;
-  return ((size_t)batch * in_features * 2 + 255) & ~size_t(255);
+constexpr int kTcMaxSplitRows = 4;
+
+// Split K so that tiles x splits fill the SMs most evenly (a wave of 148 SMs
+// over 200 tiles leaves 96 SMs idle for half the time).
+static int tc_pick_split(int ntile, int kunits, int maxs) {
+  const int sms = num_sms();
+  int ks = 1;
+  double best = 0.0;
+  for (int c = 1; c <= maxs && c <= kunits; ++c) {
+    const int units = ntile * c, waves = (units + sms - 1) / sms;
+    const double eff = (double)units / ((double)waves * sms);
+    if (eff > best + 1e-9) { best = eff; ks = c; }
+  }
+  return ks;
+}
+
+extern "C" size_t dip_int4_gemm_tc_workspace_bytes(int64_t rows, int64_t in_features, int64_t batch) {
+  if (rows <= 0 || in_features <= 0 || batch <= 0) return 0;
+  return (((size_t)batch * in_features * 2 + 255) & ~size_t(255)) +
+         (size_t)kTcMaxSplitRows * batch * rows * sizeof(float);
 }
 
 extern "C" int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
@@ -632,7 +681,7 @@ extern "C" int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, c
   if (rc) return rc;
   if (!out || !workspace) return DIP_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(workspace) & 15) return DIP_ERR_ARG;
-  if (workspace_bytes < dip_int4_gemm_tc_workspace_bytes(in_features, batch)) return DIP_ERR_WORKSPACE;
+  if (workspace_bytes < dip_int4_gemm_tc_workspace_bytes(rows, in_features, batch)) return DIP_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   // the activations with each 8-element group in the weights' dequantised order
   const int64_t n16 = batch * in_features / 8;
@@ -647,18 +696,30 @@ extern "C" int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, c
   a.R = (int)rows;
   a.K = (int)in_features;
   a.B = (int)batch;
-  a.ksplit = 1;
+  a.kgran = kTcChunkK / kTcK;
+  a.ksplit = tc_pick_split((int)((rows + kTcM - 1) / kTcM), (int)(in_features / kTcChunkK), kTcMaxSplitRows);
   a.out = out;
   a.g = g;
   a.cnt = sel_count;
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
+  if (epilogue < 0 || epilogue > 2) return DIP_ERR_ARG;
+  if (epilogue == 2 && (!g || !sel_count)) return DIP_ERR_ARG;
+  if (a.ksplit > 1) {
+    // fp32 partials of the K ranges, then one fixed-order sum with the epilogue
+    a.out_f32 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         (((size_t)batch * in_features * 2 + 255) & ~size_t(255)));
+    rc = tc_launch<kTcEpiF32, false>(a, st);
+    if (rc) return rc;
+    const int64_t n = batch * rows;
+    return launch_status(launch(tc_reduce_kernel, dim3((unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184)),
+                                dim3(256), 0, st, (const float*)a.out_f32, a.ksplit, n, epilogue,
+                                (const uint16_t*)g, sel_count, (uint16_t*)out));
+  }
   switch (epilogue) {
     case 0: return tc_launch<kTcEpiBf16, false>(a, st);
     case 1: return tc_launch<kTcEpiSilu, false>(a, st);
-    case 2:
-      if (!g || !sel_count) return DIP_ERR_ARG;
-      return tc_launch<kTcEpiH, false>(a, st);
+    case 2: return tc_launch<kTcEpiH, false>(a, st);
     default: return DIP_ERR_ARG;
   }
 }
@@ -689,15 +750,9 @@ extern "C" int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, co
   a.K = (int)inter;
   a.B = (int)batch;
   // split the channels so that tiles x splits fill the SMs most evenly (at most 8 splits)
-  const int ntile = (int)(out_features / kTcM), sms = num_sms();
-  int ks = 1;
-  double best = 0.0;
-  for (int c = 1; c <= 8 && c <= inter / kTcK; ++c) {
-    const int units = ntile * c, waves = (units + sms - 1) / sms;
-    const double eff = (double)units / ((double)waves * sms);
-    if (eff > best + 1e-9) { best = eff; ks = c; }
-  }
+  const int ks = tc_pick_split((int)(out_features / kTcM), (int)(inter / kTcK), 8);
   a.ksplit = ks;
+  a.kgran = 1;
   a.out_f32 = static_cast<float*>(workspace);
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
@@ -706,7 +761,8 @@ extern "C" int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, co
   if (rc) return rc;
   const int64_t n = batch * out_features;
   return launch_status(launch(tc_reduce_kernel, dim3((unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184)),
-                              dim3(256), 0, st, (const float*)a.out_f32, ks, n, y));
+                              dim3(256), 0, st, (const float*)a.out_f32, ks, n, (int)kTcEpiBf16,
+                              (const uint16_t*)nullptr, (const uint32_t*)nullptr, y));
 }
 
 namespace dip {

@@ -382,7 +382,7 @@ Tensor gemm_tc(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, 
     gp = bf(g);
     cp = reinterpret_cast<const uint32_t*>(cnt.data_ptr<int32_t>());
   }
-  const size_t nws = dip_int4_gemm_tc_workspace_bytes(x.size(1), x.size(0));
+  const size_t nws = dip_int4_gemm_tc_workspace_bytes(qweight.size(0), x.size(1), x.size(0));
   Tensor ws = at::empty({(int64_t)nws}, x.options().dtype(at::kByte));
   check_status(dip_int4_gemm_tc(i8(qweight), bf(scales), bf(x), qweight.size(0), x.size(1), x.size(0),
                                 (int)epilogue, gp, cp, ws.data_ptr(), nws, bfm(out), cur_stream()),

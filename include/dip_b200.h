@@ -272,9 +272,10 @@ DIP_API int dip_mlp_decode_fused_ca(const dip_layer_t* layer, const dip_ca_cache
  * h = bf16(g * bf16(acc)) * sel_count (dip_stream_predispatch.py:199-201 with
  * the token's selected channels, sel_count[b][r] = times r is in its index
  * list; 0 = not selected, h = 0), g and sel_count [batch, rows].  in_features
- * a multiple of 256; qweight, x and the workspace (a reordered copy of x,
+ * a multiple of 256; qweight, x and the workspace (a reordered copy of x and
+ * the fp32 partial sums when K is split over the SMs,
  * dip_int4_gemm_tc_workspace_bytes) 16-byte aligned, scales 4-byte aligned. */
-DIP_API size_t dip_int4_gemm_tc_workspace_bytes(int64_t in_features, int64_t batch);
+DIP_API size_t dip_int4_gemm_tc_workspace_bytes(int64_t rows, int64_t in_features, int64_t batch);
 DIP_API int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
                              int64_t rows, int64_t in_features, int64_t batch, int epilogue,
                              const dip_bf16* g, const uint32_t* sel_count, void* workspace,

@@ -70,10 +70,15 @@ def test_batched_layer_tc_matches_reference(dip, oracle, B):
     assert torch.ops.dip_b200.take_device_error() == 0
     cpu = {n: t.cpu() for n, t in L.items()}
     wg = oracle.dequantize(cpu["gate_qw"], cpu["gate_sc"])
-    g_ref = F.silu(F.linear(x.cpu(), wg))
     gc, ic, yc = g.cpu(), idx.cpu(), y.cpu()
-    err = (gc.float() - g_ref.float()).abs()
-    assert bool((err <= 2e-3 + 1e-2 * g_ref.float().abs()).all())
+    # the gate's pre-activation against F.linear(x, dequantize(W_gate)); g against
+    # SiLU of that same pre-activation (g rounds twice, so a one-ulp difference
+    # in the first rounding can move g by more than the tolerance)
+    gl = torch.ops.dip_b200.gemm_tc(L["gate_qw"], L["gate_sc"], x, 0).cpu()
+    gl_ref = F.linear(x.cpu(), wg).float()
+    assert bool(((gl.float() - gl_ref).abs() <= 2e-3 + 1e-2 * gl_ref.abs()).all())
+    g_ref = oracle.silu_bf16(gl).float()
+    assert bool(((gc.float() - g_ref).abs() <= 2e-3 + 1e-2 * g_ref.abs()).all())
     for b in (range(B) if B <= 4 else (0, 17, 63)):
         assert torch.equal(ic[b], oracle.topk_select(gc[b], cfg.k))
         il = ic[b].long()
