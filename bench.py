@@ -252,12 +252,13 @@ def run_config2(args):
 
 
 def run_tp(args):
-    """Config 4: the stack sharded along I over the N ranks of torchrun (NCCL):
-    per layer one all-gather of g (bf16, I values) and one all-reduce of the
-    fp32 [H] partials.  All N GPUs work on the same token: `value` is the
-    token rate of that one stream (strong scaling).  `comm_us_per_layer` times
-    the same two collectives alone (graph-replayed, 64 per step); they run on
-    the compute stream, so all of it is exposed."""
+    """Config 4: the stack sharded along I over the N ranks of torchrun: per
+    layer one all-gather of g (bf16, I values) and one all-reduce of the fp32
+    [H] partials, through the library's peer-memory exchange (`--comm p2p`,
+    default) or NCCL (`--comm nccl`).  All N GPUs work on the same token:
+    `value` is the token rate of that one stream (strong scaling).
+    `comm_us_per_layer` times the same two exchanges alone (graph-replayed,
+    64 per step); they run on the compute stream, so all of it is exposed."""
     rank, world, local = dist_env()
     import torch.distributed as dist
     import dip_b200  # noqa: F401
@@ -272,7 +273,7 @@ def run_tp(args):
         os.environ.setdefault("WORLD_SIZE", "1")
     dist.init_process_group("nccl", device_id=dev)
     cfg = StackConfig(n_layers=args.layers, seed=0)
-    stack = TPDipStack(cfg, dev)
+    stack = TPDipStack(cfg, dev, comm=args.comm)
     T = args.warmup + args.steps
     x0, resid = token_inputs(cfg, T, seed=1000, device=dev)
     ms, clk = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
@@ -287,7 +288,10 @@ def run_tp(args):
 
     def comm():
         for _ in range(cfg.n_layers):
-            if world > 1:
+            if world > 1 and stack.p2p is not None:
+                stack.p2p.gather(g_loc)
+                stack.p2p.reduce(part)
+            elif world > 1:
                 dist.all_gather_into_tensor(g_all, g_loc)
                 dist.all_reduce(part)
     comm_us = 0.0
@@ -320,7 +324,8 @@ def run_tp(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
             "config": {"workload": "config4: 64-layer stack sharded along I, batch 1",
-                       "layers": cfg.n_layers, "k": cfg.k, "parallelism": f"tp{world}"},
+                       "layers": cfg.n_layers, "k": cfg.k, "parallelism": f"tp{world}",
+                       "comm": args.comm},
             "us_per_layer": layer_us, "comm_us_per_layer": comm_us,
             "comm_frac_of_layer": comm_us / layer_us if layer_us else None,
             "gpu_launches": args.steps * (cfg.n_layers * 5 + cfg.n_layers - 1),
@@ -555,6 +560,8 @@ def main():
                     help="1: DIP stack (the headline line); 2: cache-aware DIP stack; "
                          "3: batched decode (--batch)")
     ap.add_argument("--batch", type=int, default=8, help="config 3: tokens per step")
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
+                    help="config 4: exchanges over peer memory (p2p) or NCCL")
     ap.add_argument("--tp", action="store_true",
                     help="config 4: shard every layer along I over the torchrun ranks")
     ap.add_argument("--single-layer", type=int, default=0, metavar="N",

@@ -26,7 +26,7 @@ LIBDIR = PKG_ROOT / "dip_b200" / "_lib"
 INCLUDE = REPO / "include"
 
 CORE_SOURCES = ["capi.cu", "gemv_int4.cu", "topk.cu", "gather_down.cu", "quant.cu",
-                "stack_ops.cu", "layer_fused.cu", "gemv_batch.cu", "gemm_tc.cu"]
+                "stack_ops.cu", "layer_fused.cu", "gemv_batch.cu", "gemm_tc.cu", "p2p.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -297,6 +297,30 @@ DIP_API int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, const
 DIP_API int dip_select_count(const int32_t* idx, int64_t batch, int64_t k, int64_t inter,
                              uint32_t* cnt, dip_stream_t stream);
 
+/* ---- tensor-parallel exchanges over peer memory (config 4) ----------------------
+ * The reference is single-GPU; the sharded layer (rank r of P owns channels
+ * [r I/P, (r+1) I/P)) needs the full g on every rank and the sum of the P fp32
+ * down partials.  These replace the NCCL all-gather / all-reduce with peer
+ * stores over NVLink into per-rank mailboxes and per-call flags.
+ * Set-up (once per rank): dip_p2p_alloc(dip_p2p_mailbox_bytes(...)) (zeroed),
+ * dip_ipc_handle of it to the peers (64 bytes), dip_ipc_open of the peers'
+ * handles.  mailboxes[q] = rank q's mailbox as this process maps it (its own
+ * for q == rank), 256-byte aligned.  Every rank must make the same sequence of
+ * calls.  dip_p2p_gather: g_local [n_local] -> the mailbox's g buffer (at byte
+ * offset 512 of the mailbox) holds all P slices in rank order.
+ * dip_p2p_reduce: y = bf16(sum over ranks in rank order of partial [hidden]),
+ * identical on every rank.  Waits are bounded (device error word on timeout). */
+DIP_API size_t dip_p2p_mailbox_bytes(int64_t inter, int64_t hidden, int64_t world);
+DIP_API int dip_p2p_alloc(size_t bytes, void** ptr);
+DIP_API int dip_p2p_free(void* ptr);
+DIP_API int dip_ipc_handle(const void* ptr, void* handle64);
+DIP_API int dip_ipc_open(const void* handle64, void** ptr);
+DIP_API int dip_ipc_close(void* ptr);
+DIP_API int dip_p2p_gather(int rank, int world, void* const* mailboxes, const dip_bf16* g_local,
+                           int64_t n_local, int64_t hidden, dip_stream_t stream);
+DIP_API int dip_p2p_reduce(int rank, int world, void* const* mailboxes, const float* partial,
+                           int64_t inter, int64_t hidden, dip_bf16* y, dip_stream_t stream);
+
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit
  * exact with scripts/quantize.py:32-64. */
