@@ -1018,10 +1018,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   for (int u = 0; u < GW; ++u)
 #pragma unroll
     for (int m = 0; m < 8; ++m) acc[u][m][0] = acc[u][m][1] = acc[u][m][2] = acc[u][m][3] = 0.f;
-  float colsum[GW];
-#pragma unroll
-  for (int u = 0; u < GW; ++u) colsum[u] = 0.f;
-  const int tpair = lane & 7, twhich = (lane >> 3) & 1;
+  // B values: lane l computes group ub = l / 16 (GW == 2; lanes 0-15 when
+  // GW == 1), channel pair l & 7, hi or lo part (l / 8) & 1, so both groups'
+  // values come from one pass of the whole warp
+  float colsum = 0.f;
+  const int tpair = lane & 7, twhich = (lane >> 3) & 1, ub = (GW == 2) ? (lane >> 4) : 0;
   for (int j = nC; j < nC + nD; ++j) {
     cp_wait_lf2();
     __syncwarp();
@@ -1031,24 +1032,24 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     if (j == nC) LF_CTA(17);
     const uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
     const int i = j - nC;
+    uint32_t bval = 0;
+    if (GW == 2 || lane < 16) {
+      float v2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 2 * tpair + e;
+        const uint16_t* sp = reinterpret_cast<const uint16_t*>(slot + 16 * kLfDnPitch + c * 4);
+        const int sidx = (GW == 1) ? (warp & 1) : ub;
+        const float hs = dh[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
+        const float h1 = round_bf16(hs);
+        v2[e] = twhich ? round_bf16(hs - h1) : h1;
+      }
+      colsum += v2[0] + v2[1];
+      bval = (uint32_t)f32_to_bf16_bits(v2[0]) | ((uint32_t)f32_to_bf16_bits(v2[1]) << 16);
+    }
 #pragma unroll
     for (int u = 0; u < GW; ++u) {
-      uint32_t bval = 0;
-      if (lane < 16) {
-        float v2[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = 2 * tpair + e;
-          const uint16_t* sp = reinterpret_cast<const uint16_t*>(slot + 16 * kLfDnPitch + c * 4);
-          const int sidx = (GW == 1) ? (warp & 1) : u;
-          const float hs = dh[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
-          const float h1 = round_bf16(hs);
-          v2[e] = twhich ? round_bf16(hs - h1) : h1;
-        }
-        colsum[u] += v2[0] + v2[1];
-        bval = (uint32_t)f32_to_bf16_bits(v2[0]) | ((uint32_t)f32_to_bf16_bits(v2[1]) << 16);
-      }
-      const int src = (gq & 1) * 8;
+      const int src = (gq & 1) * 8 + 16 * u;
       const uint32_t b0 = __shfl_sync(0xffffffffu, bval, src + tq);
       const uint32_t b1 = __shfl_sync(0xffffffffu, bval, src + tq + 4);
       const uint8_t* base = slot + u * 64 + gq * 8;
@@ -1078,10 +1079,10 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   LF_CTA(4);
 #pragma unroll
   for (int u = 0; u < GW; ++u) {
-    float cs = colsum[u];
+    float cs = colsum;
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-    const float bias_d = kNibbleBias * __shfl_sync(0xffffffffu, cs, 0);
+    const float bias_d = kNibbleBias * __shfl_sync(0xffffffffu, cs, 16 * u);
     if (tq == 0) {
       float* dst = a.partial + (size_t)b * H + (warp * GW + u) * kGroup + gq * 16;
       float v[16];
