@@ -1,4 +1,4 @@
-"""Benchmark: Qwen3-32B-shaped DIP decode MLP stack.
+"""Benchmark: Qwen3-32B-shaped DIP decode MLP stack (BASELINE configs 1 and 4).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -7,6 +7,12 @@ A step is one decode token through the 64-layer int4 DIP MLP stack at batch 1
 resident in HBM, replayed from a CUDA graph.  Every step reads ~9.5 GB of
 weights, far more than the 126 MB L2, so no L2 flush is needed.  Prints one
 JSON line (rank 0).
+
+One GPU: config 1, one layer_fused_kernel launch per layer.  Under torchrun
+with N > 1 ranks: config 4, the same token stream with every layer sharded
+along I over the N GPUs (one dip_mlp_decode_fused_tp launch per layer and
+rank; strong scaling), checked in the run against one GPU's indices.
+`--replicas` instead runs N independent single-GPU stacks.
 
 --impl reference times the reference's own CPU math for the same layer
 (dequantise per call, F.linear, SiLU, the topk_select.cu selection, row
@@ -126,28 +132,43 @@ def cpu_reference_layer_time(n_layers_sample: int, seed: int = 0, layer=None):
 
 
 def run_reference(args):
+    """The reference's own math for this path (dequantise per call, F.linear,
+    SiLU, the topk_select.cu selection, row gather, matmul) on the host cores,
+    through the CPU port in oracle/ (the reference's CUDA kernels are sm_75
+    code with host round trips; its CPU path is plain torch).  A step here is
+    a bounded sample of 2 layers of the 64-layer token; the token rate is
+    extrapolated as 1 / (64 x seconds per layer).  Under torchrun only rank 0
+    runs; the CPU math does not shard over GPUs, so the same sample stands for
+    every N."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     per_step_layers = 2
-    # steps are bounded samples: each step = 2 layers of the 64-layer token
     from oracle import dip_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     layer = O.make_layer_cpu(5120, 25600, seed=0)
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_reference_layer_time(1, layer=layer)
-    sec, cores = cpu_reference_layer_time(per_step_layers * args.steps, layer=layer)
+    n_layers = per_step_layers * args.steps
+    sec, cores = cpu_reference_layer_time(n_layers, layer=layer)
     tok_s = 1.0 / (64 * sec)
-    sample = (f"{per_step_layers * args.steps} config-1 layers (hidden 5120, inter 25600, "
-              f"k 15360) of the reference CPU math; tok/s = 1/(64 x s/layer)")
+    sample = (f"{n_layers} config-1 layers (hidden 5120, inter 25600, k 15360) of the "
+              f"reference CPU math on {cores} threads; tok/s = 1/(64 x s/layer)")
+    cfg = {"workload": ("config1: 64-layer Qwen3-32B-shape DIP decode MLP stack, batch 1"
+                        if world == 1 else
+                        f"config4: the config-1 stack sharded along I over {world} GPUs, batch 1"),
+           "hidden": 5120, "inter": 25600, "k": 15360, "layers": 64, "keep_ratio": 0.6,
+           "parallelism": "single" if world == 1 else f"tp{world}",
+           "l2": "no flush: each step reads ~9.5 GB of weights (> 126 MB L2)"}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 64 * sec * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": "config1 64-layer DIP MLP stack, batch 1 (CPU sample)",
-                   "hidden": 5120, "inter": 25600, "k": 15360, "layers": 64},
+        "higher_is_better": True, "scaling": "weak" if world == 1 else "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": cfg,
         "us_per_layer": sec * 1e6,
+        "layers_timed": n_layers, "step_definition": f"{per_step_layers} layers per step",
+        "extrapolated_to": "64 x s/layer per token (ms_per_step is that extrapolation)",
         "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -192,7 +213,7 @@ def _time_stack(stack, x0, resid, warmup, steps, dev):
     return e0.elapsed_time(e1) / steps, clk.summary()
 
 
-def run_config2(args):
+def run_config2(args, emit=True):
     """Config 2: cache-aware DIP on the 64-layer stack with LogNormal(0,1)
     gate-row scales; calibration on 32 N(0,1) tokens run through the DIP
     stack, cache_n = 0.3 I hot channels per layer.  Reports us/layer and
@@ -234,7 +255,8 @@ def run_config2(args):
     stack.mode, stack.fused, stack._graph = "fused", True, None
     ms_fused, _ = _time_stack(stack, x0, resid, args.warmup, args.steps, dev)
     us_ca = ms_ca * 1e3 / cfg.n_layers
-    print(json.dumps({
+    del stack
+    rec = {
         "metric": "dip_ca_mlp_decode_tok_s", "value": 1e3 / ms_ca, "unit": "tok/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_ca,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -248,7 +270,10 @@ def run_config2(args):
         "ca_separate_launches_us_per_layer": ms_chain * 1e3 / cfg.n_layers,
         "streaming_fused_us_per_layer_same_weights": ms_fused * 1e3 / cfg.n_layers,
         "gpu_launches": args.steps * cfg.n_layers,
-        "clocks": clk}), flush=True)
+        "clocks": clk}
+    if emit:
+        print(json.dumps(rec), flush=True)
+    return rec
 
 
 def run_tp(args):
@@ -281,6 +306,8 @@ def run_tp(args):
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = tt.item()
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out during the timed steps: run invalid")
     # the collectives alone
     g_loc = torch.zeros(cfg.inter // world, dtype=torch.bfloat16, device=dev)
     g_all = torch.zeros(cfg.inter, dtype=torch.bfloat16, device=dev)
@@ -316,6 +343,8 @@ def run_tp(args):
         ct = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
         dist.all_reduce(ct, op=dist.ReduceOp.MAX)
         comm_us = ct.item() * 1e3 / cfg.n_layers
+        if _device_error_all(world, dev):
+            raise SystemExit("a bounded device wait ran out in the exchange timing: run invalid")
     layer_us = ms * 1e3 / cfg.n_layers
     if rank == 0:
         print(json.dumps({
@@ -347,7 +376,7 @@ def _free_port():
     return port
 
 
-def run_config3(args):
+def run_config3(args, emit=True):
     """Config 3: B independent tokens per step through the 64-layer stack
     (per-token DIP selection; `--path tc` (default) streams every weight once
     for the batch through the tcgen05 GEMMs, `--path gather` gathers each
@@ -390,7 +419,8 @@ def run_config3(args):
         launches = passes + 1 + 2 * B + 1
     layer_us = ms * 1e3 / cfg.n_layers
     peak, peak_kind = _peaks()
-    print(json.dumps({
+    del stack
+    rec = {
         "metric": "dip_mlp_decode_tok_s", "value": B * 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -401,11 +431,98 @@ def run_config3(args):
         "layer_bytes": layer_bytes, "layer_hbm_gbs": layer_bytes / (layer_us * 1e-6) / 1e9,
         "layer_hbm_frac": layer_bytes / (layer_us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
         "gpu_launches": args.steps * cfg.n_layers * launches,
-        "clocks": clk}), flush=True)
+        "clocks": clk}
+    if emit:
+        print(json.dumps(rec), flush=True)
+    return rec
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed_replays(stack, x0, resid, warmup, steps, dev, world):
+    """Graph replays: `warmup` untimed, then `steps` between a barrier +
+    synchronize on both sides, timed with CUDA events on the replay stream;
+    returns (ms per step, max over ranks; clock summary)."""
+    stack.capture()
+    xi, ri = stack._static_in
+    for t in range(warmup):
+        xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+    torch.cuda.synchronize()
+    _barrier(world); torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record()
+        for t in range(warmup, warmup + steps):
+            xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    _barrier(world); torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    return ms / steps, clk.summary()
+
+
+def _e2e(stack, x0, resid, warmup, steps, dev, world, n_layers, hidden):
+    """The public call (stack.decode) with pinned host inputs and a host
+    result every step: H2D of the token and its 64 residuals, D2H of y."""
+    x0h = x0.cpu().pin_memory()
+    rh = resid.cpu().pin_memory()
+    for t in range(min(3, warmup)):
+        stack.decode(x0h[t], rh[t])
+    _barrier(world); torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for t in range(warmup, warmup + steps):
+        stack.decode(x0h[t], rh[t])
+    torch.cuda.synchronize()
+    e2e_s = _max_over_ranks(time.perf_counter() - t0, world, dev)
+    return {"value": steps / e2e_s, "unit": UNIT,
+            "h2d_bytes_per_step": (x0[0].numel() + resid[0].numel()) * 2,
+            "d2h_bytes_per_step": hidden * 2}
+
+
+def _device_error_all(world, dev) -> int:
+    """The library's device error word, OR-ed over the ranks (a bounded wait
+    that ran out anywhere makes the run invalid)."""
+    err = int(torch.ops.dip_b200.take_device_error())
+    return int(_max_over_ranks(float(err), world, dev))
+
+
+def _config1(cfg, world, parallelism):
+    return {"workload": ("config1: 64-layer Qwen3-32B-shape DIP decode MLP stack, batch 1"
+                         if world == 1 else
+                         f"config4: the config-1 stack sharded along I over {world} GPUs, batch 1"),
+            "hidden": cfg.hidden, "inter": cfg.inter, "k": cfg.k, "layers": cfg.n_layers,
+            "keep_ratio": cfg.keep_ratio, "parallelism": parallelism,
+            "l2": "no flush: each step reads ~9.5 GB of weights (> 126 MB L2)"}
+
+
+def _roofline(kern, alg_bytes, layer_us, traffic, peak, peak_kind):
+    """The dominant kernel is the whole layer (one launch per layer), so its
+    duration per launch is the graph-replayed step time / layers: the launch
+    plus the gap to the next one (an upper bound on the kernel time)."""
+    achieved = alg_bytes / (layer_us * 1e-6) / 1e9
+    return {"kernel": kern, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": f"{peak_kind} (burst copy)",
+            "traffic": traffic, "algorithmic_bytes": alg_bytes, "avg_launch_us": layer_us,
+            "launch_time_from": "graph-replayed timed region: ms_per_step / layers"}
 
 
 def run_ours(args):
     rank, world, local = dist_env()
+    if world > 1 and not args.replicas:
+        return run_tp_fused(args)
     import dip_b200  # noqa: F401  (loads the kernels; raises if unbuilt)
     from dip_b200.stack import StackConfig, DipStack, token_inputs, layer_weight_bytes
 
@@ -418,119 +535,38 @@ def run_ours(args):
     stack = DipStack(cfg, dev, fused=(args.path == "fused"))
     T = args.warmup + args.steps
     x0, resid = token_inputs(cfg, T, seed=1000 + rank, device=dev)
-    stack.capture()
-    xi, ri = stack._static_in
+    ms_per_step, clk = _timed_replays(stack, x0, resid, args.warmup, args.steps, dev, world)
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out during the timed steps: run invalid")
+    value = world * 1e3 / ms_per_step
+    e2e = _e2e(stack, x0, resid, args.warmup, args.steps, dev, world, cfg.n_layers, cfg.hidden)
+    e2e["value"] *= world
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-
-    # warm-up
-    for t in range(args.warmup):
-        xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
-    torch.cuda.synchronize()
-    barrier(); torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record()
-        for t in range(args.warmup, T):
-            xi.copy_(x0[t]); ri.copy_(resid[t]); stack.replay()
-        e1.record()
-        torch.cuda.synchronize()
-    barrier(); torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = tt.item()
-    ms_per_step = ms / args.steps
-    value = world * args.steps / (ms / 1e3)
-
-    # e2e through the public call with host buffers (H2D in, D2H out, every step)
-    x0h = x0.cpu().pin_memory()
-    rh = resid.cpu().pin_memory()
-    for t in range(min(3, args.warmup)):
-        stack.decode(x0h[t], rh[t])
-    barrier(); torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for t in range(args.warmup, T):
-        stack.decode(x0h[t], rh[t])
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = tt.item()
-    e2e = {"value": world * args.steps / e2e_s, "unit": UNIT,
-           "h2d_bytes_per_step": (x0[0].numel() + resid[0].numel()) * 2,
-           "d2h_bytes_per_step": cfg.hidden * 2}
-
-    # dominant kernel, timed per launch with CUDA events on the launching stream
     nb = layer_weight_bytes(cfg)
-    xg = x0[0].contiguous()
-    evs = []
-    if stack.fused:
-        # the whole layer is one launch (layer_fused_kernel): every byte the
-        # layer must read is this kernel's algorithmic traffic
-        kern = "layer_fused_kernel (one decode layer: gate, exact top-k, gathered up/down)"
-        alg_bytes = nb["total"]
-        ws = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(cfg.hidden, cfg.inter,
-                                                                      cfg.k),
-                         dtype=torch.uint8, device=dev)
-
-        def one(L):
-            torch.ops.dip_b200.mlp_decode_fused(L["gate_qw"], L["gate_sc"], L["up_qw"],
-                                                L["up_sc"], L["down_t_qw"], L["down_t_sc"],
-                                                xg, None, 1e-6, cfg.k, ws)
-        traffic_key = "layer_fused_kernel"
-    else:
-        kern = "gate_silu (int4 GEMV + SiLU, 25600x5120)"
-        alg_bytes = nb["gate"]
-
-        def one(L):
-            torch.ops.dip_b200.gate_silu(L["gate_qw"], L["gate_sc"], xg)
-        traffic_key = "gate_silu"
-    for rep in range(3):
-        for L in stack.layers:  # 64 distinct layers: each launch reads cold weights
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            one(L)
-            b.record()
-            evs.append((a, b))
-    torch.cuda.synchronize()
-    durs = [a.elapsed_time(b) for a, b in evs[len(stack.layers):]]
-    kern_avg_ms = sum(durs) / len(durs)
     peak, peak_kind = _peaks()
-    achieved = alg_bytes / (kern_avg_ms / 1e3) / 1e9
-    traffic = _traffic().get(traffic_key)
     layer_us = ms_per_step * 1e3 / cfg.n_layers
     layer_gbs = nb["total"] / (layer_us / 1e6) / 1e9
-
+    if stack.fused:
+        kern = "layer_fused_kernel (one decode layer: gate, exact top-k, gathered up/down)"
+        roof = _roofline(kern, nb["total"], layer_us, _traffic().get("layer_fused_kernel"), peak,
+                         peak_kind)
+    else:
+        roof = None
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
-        "config": {"workload": "config1: 64-layer Qwen3-32B-shape DIP decode MLP stack, batch 1",
-                   "hidden": cfg.hidden, "inter": cfg.inter, "k": cfg.k, "layers": cfg.n_layers,
-                   "keep_ratio": cfg.keep_ratio, "parallelism": f"replicas{world}",
-                   "l2": "no flush: each step reads ~9.5 GB of weights (> 126 MB L2)"},
+        "config": _config1(cfg, 1, "single" if world == 1 else f"replicas{world}"),
         "us_per_layer": layer_us,
         "layer_hbm_gbs": layer_gbs,
         "layer_hbm_frac_of_measured": layer_gbs / peak,
         "layer_hbm_frac_of_8tbs": layer_gbs / 8000.0,
-        "roofline": {"kernel": kern, "bound": "hbm",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (burst copy)",
-                     "traffic": traffic, "algorithmic_bytes": alg_bytes,
-                     "avg_launch_us": kern_avg_ms * 1e3},
+        "roofline": roof,
         "e2e": e2e,
         "gpu_launches": args.steps * (cfg.n_layers if stack.fused else cfg.n_layers * 6 - 1),
         "path": args.path,
-        "clocks": clk.summary(),
+        "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # bounded CPU sample on layer 0's own weights
@@ -540,11 +576,126 @@ def run_ours(args):
             "value": 1.0 / (64 * sec), "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{args.cpu_layers} layers of the reference CPU math on layer 0's "
                       f"weights; tok/s = 1/(64 x {sec:.3f} s/layer)"}
+    if rank == 0 and world == 1 and args.subresults:
+        del stack
+        torch.cuda.empty_cache()
+        line["subresults"] = _subresults(args, dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_tp_fused(args):
+    """Config 4: one token stream, every layer sharded along I over the N
+    ranks, one dip_mlp_decode_fused_tp launch per layer and rank.  After the
+    timed steps: one recorded token whose per-layer indices (all ranks'
+    entries) rank 0 compares with the single-GPU fused layer on the full
+    weights and the same layer inputs (tp_idx_exact), and the same shards
+    timed with no exchange at all (each rank alone on its rows, k / N) to
+    give the exposed cost of the cross-GPU steps."""
+    rank, world, local = dist_env()
+    import torch.distributed as dist
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, DipStack, token_inputs, layer_weight_bytes, RMS_EPS
+    from dip_b200.tp import TPFusedStack
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    cfg = StackConfig(n_layers=args.layers, seed=0)
+    stack = TPFusedStack(cfg, dev, keep_full=(rank == 0))
+    T = args.warmup + args.steps
+    x0, resid = token_inputs(cfg, T, seed=1000, device=dev)
+    ms_per_step, clk = _timed_replays(stack, x0, resid, args.warmup, args.steps, dev, world)
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out during the timed steps: run invalid")
+    e2e = _e2e(stack, x0, resid, args.warmup, args.steps, dev, world, cfg.n_layers, cfg.hidden)
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out during the e2e steps: run invalid")
+
+    # in-run parity against one GPU: the first timed token, recorded
+    stack.step(x0[args.warmup], resid[args.warmup], record=True)
+    torch.cuda.synchronize()
+    exact, y_ok, n_bad = True, True, 0
+    if rank == 0:
+        ws1 = torch.zeros(torch.ops.dip_b200.mlp_fused_workspace_bytes(cfg.hidden, cfg.inter, cfg.k),
+                          dtype=torch.uint8, device=dev)
+        for l in range(cfg.n_layers):
+            L = stack.full[l]
+            y1, _, idx1 = torch.ops.dip_b200.mlp_decode_fused(
+                L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
+                L["down_t_sc"], stack.last_x[l], None, RMS_EPS, cfg.k, ws1)
+            if not torch.equal(idx1, stack.last_idx[l]):
+                exact = False
+                n_bad += 1
+        del ws1
+    flag = torch.tensor([0 if exact else 1], device=dev)
+    dist.broadcast(flag, 0)
+    exact = flag.item() == 0
+
+    # the same shards with no cross-GPU step: each rank alone on its rows
+    stack.full = None
+    torch.cuda.empty_cache()
+    cfg_loc = StackConfig(n_layers=cfg.n_layers, inter=cfg.inter // world, seed=0)
+    local_stack = DipStack(cfg_loc, dev, layers=stack.shards)
+    ms_loc, _ = _timed_replays(local_stack, x0, resid, args.warmup, args.steps, dev, world)
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out in the local-only timing: run invalid")
+
+    nb = layer_weight_bytes(cfg)
+    peak, peak_kind = _peaks()
+    layer_us = ms_per_step * 1e3 / cfg.n_layers
+    loc_us = ms_loc * 1e3 / cfg.n_layers
+    per_gpu_bytes = nb["total"] // world
+    line = {
+        "metric": METRIC, "value": 1e3 / ms_per_step, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
+        "config": _config1(cfg, world, f"tp{world}"),
+        "us_per_layer": layer_us,
+        "per_gpu_hbm_gbs": per_gpu_bytes / (layer_us * 1e-6) / 1e9,
+        "per_gpu_hbm_frac_of_measured": per_gpu_bytes / (layer_us * 1e-6) / 1e9 / peak,
+        "tp_idx_exact": exact, "tp_idx_layers_checked": cfg.n_layers,
+        "tp_idx_layers_differing": n_bad,
+        "local_only_us_per_layer": loc_us,
+        "comm_us_per_layer": layer_us - loc_us,
+        "comm_frac_of_layer": (layer_us - loc_us) / layer_us,
+        "comm_note": ("exposed cost of the cross-GPU steps inside the fused TP kernel (remote "
+                      "histogram increments, count words, y-slot exchange, waiting for the "
+                      "slowest rank) = TP layer time - the same shards run alone with k/N"),
+        "roofline": _roofline("layer_fused_kernel<TP> (one sharded decode layer per rank)",
+                              per_gpu_bytes, layer_us, None, peak, peak_kind),
+        "e2e": e2e,
+        "gpu_launches": args.steps * cfg.n_layers,
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    sys.stdout.flush()
+    code = 0 if exact else 3
+    if rank == 0 and not exact:
+        print(f"tensor-parallel indices differ from one GPU's on {n_bad} layers", file=sys.stderr)
+    os._exit(code)
+
+
+def _subresults(args, dev):
+    """Short sub-runs recorded in the headline line: config 2 (cache-aware
+    DIP, hit rate and split exactness) and config 3 (batch 64 through the
+    tcgen05 GEMMs)."""
+    import argparse as _ap
+    out = {}
+    sub = _ap.Namespace(**vars(args))
+    sub.steps, sub.warmup = args.sub_steps, 3
+    out["config2"] = run_config2(sub, emit=False)
+    torch.cuda.empty_cache()
+    sub.batch, sub.path = 64, "tc"
+    out["config3_b64"] = run_config3(sub, emit=False)
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -563,7 +714,13 @@ def main():
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="config 4: exchanges over peer memory (p2p) or NCCL")
     ap.add_argument("--tp", action="store_true",
-                    help="config 4: shard every layer along I over the torchrun ranks")
+                    help="config 4 as separate launches (gate, top-k, up, down, exchange "
+                         "kernels or NCCL, --comm) over the torchrun ranks")
+    ap.add_argument("--replicas", action="store_true",
+                    help="under torchrun: N independent single-GPU stacks instead of config 4")
+    ap.add_argument("--no-subresults", dest="subresults", action="store_false",
+                    help="skip the config-2 and config-3 sub-runs of the one-GPU line")
+    ap.add_argument("--sub-steps", type=int, default=8)
     ap.add_argument("--single-layer", type=int, default=0, metavar="N",
                     help="profiling aid: N launches of one config-1 fused layer, then exit")
     ap.add_argument("--path", default="fused", choices=["fused", "chain", "tc", "gather"],

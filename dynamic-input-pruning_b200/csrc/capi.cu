@@ -9,7 +9,9 @@
 
 namespace dip {
 
-__device__ unsigned int dip_error_word = 0;
+// Device control block: word 0 = error bits (kErrTimeout, ...), word 1 =
+// poll limit of the bounded waits (0 = the compiled default).
+__device__ unsigned int dip_device_ctl[2] = {0u, 0u};
 
 static std::atomic<int> g_pdl{1};
 static std::atomic<int> g_simple_gemv{0};
@@ -18,16 +20,22 @@ static thread_local char g_last_err[256] = "";
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 bool force_simple_gemv() { return g_simple_gemv.load(std::memory_order_relaxed) != 0; }
 
+// The address is looked up once per device (host threads may race on the
+// first call: every racer stores the same value).  It stays valid while the
+// device's primary context lives; after cudaDeviceReset the library must be
+// reloaded.
 unsigned* error_word_ptr() {
-  static unsigned* cache[64] = {};
+  static std::atomic<unsigned*> cache[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cache[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, dip_error_word) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<unsigned*>(p);
+  unsigned* p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* q = nullptr;
+    if (cudaGetSymbolAddress(&q, dip_device_ctl) != cudaSuccess) return nullptr;
+    p = static_cast<unsigned*>(q);
+    cache[dev].store(p, std::memory_order_release);
   }
-  return cache[dev];
+  return p;
 }
 
 int launch_status(cudaError_t e) {
@@ -76,9 +84,14 @@ extern "C" int dip_set_gemv_variant(int simple) { return g_simple_gemv.exchange(
 extern "C" int dip_take_device_error(unsigned int* out) {
   if (!out) return DIP_ERR_ARG;
   unsigned int zero = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(out, dip_error_word, sizeof(unsigned int));
+  cudaError_t e = cudaMemcpyFromSymbol(out, dip_device_ctl, sizeof(unsigned int));
   if (e != cudaSuccess) return launch_status(e);
-  return launch_status(cudaMemcpyToSymbol(dip_error_word, &zero, sizeof(unsigned int)));
+  return launch_status(cudaMemcpyToSymbol(dip_device_ctl, &zero, sizeof(unsigned int)));
+}
+
+extern "C" int dip_set_spin_limit(unsigned int polls) {
+  return launch_status(cudaMemcpyToSymbol(dip_device_ctl, &polls, sizeof(unsigned int),
+                                          sizeof(unsigned int)));
 }
 
 extern "C" size_t dip_mlp_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {

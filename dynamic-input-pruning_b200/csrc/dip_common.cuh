@@ -154,6 +154,11 @@ static_assert(sizeof(GridBar) == 256, "grid barrier words occupy 256 bytes of wo
 // Test switch: route the GEMV family through the simple (non-ring) kernel.
 bool force_simple_gemv();
 
+// Bytes from `p` to the end of a device allocation this library made with
+// dip_p2p_alloc or mapped with dip_ipc_open (0 when `p` lies in neither):
+// the bound every peer-memory store of an exchange is checked against.
+size_t p2p_registered_bytes(const void* p);
+
 // Device address of the library's error word on the current device (looked
 // up once per device with cudaGetSymbolAddress); nullptr on failure.
 unsigned* error_word_ptr();
@@ -186,6 +191,13 @@ namespace dip {
 #endif
 constexpr uint32_t kSpinLimit = DIP_SPIN_LIMIT;
 constexpr unsigned kErrTimeout = 1u;
+// `err` points at the library's device control block (error_word_ptr):
+// word 0 holds the error bits, word 1 the poll limit of the bounded waits
+// (0: kSpinLimit; set with dip_set_spin_limit).
+__device__ __forceinline__ uint32_t spin_limit(const unsigned* err) {
+  const unsigned v = err ? *reinterpret_cast<const volatile unsigned*>(err + 1) : 0u;
+  return v ? v : kSpinLimit;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -217,7 +229,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait; returns false (and flags the error) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  for (uint32_t i = 0, lim = spin_limit(err); i < lim; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   atomicOr(err, kErrTimeout);
   return false;
@@ -250,7 +262,7 @@ __device__ __forceinline__ void grid_sync(GridBar* b, unsigned* err) {
       atomicAdd(&b->gen, 1u);
     } else {
       bool done = false;
-      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+      for (uint32_t it = 0, lim = spin_limit(err); it < lim && !done; ++it) {
         unsigned g;
         asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(&b->gen) : "memory");
         done = (g != g0);

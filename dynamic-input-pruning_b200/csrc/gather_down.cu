@@ -17,6 +17,8 @@
 // 2^23 + u*16^i; after XOR with 8 (two's complement -> offset binary) and a
 // paired subtraction, the paired FMA (sm_100 FFMA2) multiplies by
 // h*s*16^-i, which is exact because h*s (bf16 x bf16) has 16 significant bits.
+#include <atomic>
+
 #include "dip_common.cuh"
 
 namespace dip {
@@ -566,17 +568,22 @@ static __device__ __align__(256) float g_noalloc_partials[kDownCtas * kNoAllocMa
 
 // Device address of g_noalloc_partials on the current device.  In host code
 // the array's name is only a host-side stand-in, so the real address is
-// looked up once per device (with that device current) and cached.
+// looked up once per device (with that device current) and cached in an
+// atomic slot (concurrent first calls from several host threads store the
+// same value).  The cached address is valid while the device's primary
+// context lives; after cudaDeviceReset the library must be reloaded.
 static float* noalloc_partials_ptr() {
-  static float* cache[64] = {};
+  static std::atomic<float*> cache[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cache[dev]) {
+  float* p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_partials) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<float*>(ptr);
+    p = static_cast<float*>(ptr);
+    cache[dev].store(p, std::memory_order_release);
   }
-  return cache[dev];
+  return p;
 }
 
 extern "C" int dip_int4_gather_down_noalloc(const int8_t* down_t, const dip_bf16* scales,

@@ -28,7 +28,7 @@
 // and a tail; here the CTAs stay resident (one per SM, cooperative launch),
 // the x fragments of the CTA's K-slice are loaded once and used by both GEMVs,
 // and the up and down rows of a channel are read by the same CTA.  Each warp
-// streams its bytes through a private 4-deep cp.async ring and never waits for
+// streams its bytes through a private 3-deep cp.async ring and never waits for
 // another warp inside a phase.  The gate phase's first tiles are requested
 // before waiting on the previous kernel (weights are static), so consecutive
 // layers overlap.
@@ -36,39 +36,6 @@
 #include "dip_common.cuh"
 
 namespace dip {
-
-// Phase tracing (compile with -DDIP_TRACE): thread 0 of CTA 1 records the
-// global timer at phase boundaries into dip_lf_trace[]; thread 0 of every CTA
-// records the global timer at the points of dip_lf_cta[][].
-#ifdef DIP_TRACE
-__device__ unsigned long long dip_lf_trace[16];
-__device__ unsigned long long dip_lf_cta[160][32];
-__device__ unsigned long long dip_lf_tile[160][64];
-}  // namespace dip
-extern "C" void dip_lf_tile_read(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, dip::dip_lf_tile, 160 * 64 * sizeof(unsigned long long));
-}
-extern "C" void dip_lf_trace_read(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, dip::dip_lf_trace, 16 * sizeof(unsigned long long));
-}
-extern "C" void dip_lf_cta_read(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, dip::dip_lf_cta, 160 * 32 * sizeof(unsigned long long));
-}
-namespace dip {
-#define LF_TRACE(n) \
-  do { if (threadIdx.x == 0 && blockIdx.x == 1) { unsigned long long t; \
-       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_trace[n] = t; } } while (0)
-#define LF_CTA(n) \
-  do { if (threadIdx.x == 0) { unsigned long long t; \
-       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_cta[blockIdx.x][n] = t; } } while (0)
-#define LF_TILE(n) \
-  do { if (threadIdx.x == 0 && (n) < 64) { unsigned long long t; \
-       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); dip_lf_tile[blockIdx.x][n] = t; } } while (0)
-#else
-#define LF_TRACE(n) do { } while (0)
-#define LF_TILE(n) do { } while (0)
-#define LF_CTA(n) do { } while (0)
-#endif
 
 constexpr int kLfWarps = 20;
 constexpr int kLfThreads = kLfWarps * 32;
@@ -78,7 +45,10 @@ constexpr int kLfThreads = kLfWarps * 32;
 constexpr int kLfDepth = DIP_LF_DEPTH;  // cp.async ring slots per warp
 constexpr int kLfTilesA = 12;   // max gate tiles (16 rows) per CTA
 constexpr int kLfDnPitch = 144;  // bytes per channel row of a down slot (128 + pad)
+constexpr int kLfMaxCtas = 160;  // CTAs per grid (SMs per GPU) supported
+constexpr int kLfMaxRanks = 8;   // tensor-parallel ranks supported
 
+struct LfSel;
 struct LfArgs {
   const uint8_t* gate_qw; const uint16_t* gate_sc;
   const uint8_t* up_qw; const uint16_t* up_sc;
@@ -101,6 +71,15 @@ struct LfArgs {
   const int64_t* id2slot;
   const uint8_t* res_up_qw; const uint16_t* res_up_sc;
   const uint8_t* res_dn_qw; const uint16_t* res_dn_sc;
+  // tensor parallel along I (template TP): this rank's rows are the channels
+  // [c0, c0 + inter) of inter_total.  psel / pysl / pyflag[q]: rank q's
+  // selection block, y slots [world][hidden] fp32 and y flags [world][160],
+  // as this rank maps them (q == rank: its own).  Single GPU: inter_total =
+  // inter, rank 0, world 1, c0 0.
+  int inter_total, rank, world, c0;
+  LfSel* psel[kLfMaxRanks];
+  float* pysl[kLfMaxRanks];
+  unsigned long long* pyflag[kLfMaxRanks];
 };
 
 // Byte offsets of the dynamic shared memory.
@@ -244,7 +223,6 @@ __device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, QRow qrow, SRow sro
 
 // Selection parameters of one call, written by the coordinating CTA (CTA 0)
 // once every worker has arrived, read by the workers.
-constexpr int kLfMaxCtas = 160;
 // Words written once per call carry the call's tag (bit 31 set, never 0) in
 // their upper half, so a reader polls the word itself and needs no separate
 // flag: 64-bit stores and loads are single-copy atomic.
@@ -257,8 +235,12 @@ struct LfSel {
   unsigned pad0[31];
   unsigned long long par[4];             // tagged: lo bits, hi bits, totA, filled
   unsigned long long pre[kLfMaxCtas][2];  // tagged, per worker: tier A, tier B counts before it
-  unsigned long long cnt[kLfMaxCtas];     // per worker: 1<<63 | tier A << 32 | tier B; zero between calls
-  unsigned fine[kTopkHistBins];  // fine |g| histogram (one bin per key); zero between calls
+  // tagged, per rank and worker: tier A << 16 | tier B (single GPU: rank 0)
+  unsigned long long cnt[kLfMaxRanks][kLfMaxCtas];
+  // fine |g| histogram (one bin per key).  Single GPU: set 0 only, zero
+  // between calls.  Tensor parallel: set (call index & 1); a call clears the
+  // other set, which the previous call used (see layer_fused_kernel).
+  unsigned fine[2][kTopkHistBins];
 };
 static_assert(offsetof(LfSel, coarse) % 16 == 0 && offsetof(LfSel, fine) % 16 == 0,
               "histograms are read in 16-byte pieces");
@@ -281,7 +263,7 @@ __device__ __forceinline__ void lf_final_barrier(unsigned long long* done, unsig
     asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;\n" : "=l"(old) : "l"(done) : "memory");
     const unsigned long long target = old - old % nb + nb;
     bool ok = old + 1 == target;
-    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+    for (uint32_t it = 0, lim = spin_limit(err); it < lim && !ok; ++it) {
       unsigned long long v;
       asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(done) : "memory");
       ok = v >= target;
@@ -299,6 +281,37 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// System-scope forms for words that other GPUs write over NVLink (TP).
+__device__ __forceinline__ unsigned ld_relaxed_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const unsigned* p) {  // 16-byte aligned
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+template <bool TP>
+__device__ __forceinline__ unsigned lf_ld_u32(const unsigned* p) {
+  return TP ? ld_relaxed_sys_u32(p) : ld_relaxed_u32(p);
+}
+template <bool TP>
+__device__ __forceinline__ uint4 lf_ld_v4(const unsigned* p) {
+  return TP ? ld_relaxed_sys_v4(p) : ld_relaxed_v4(p);
+}
 
 // Gate rows of worker CTA b (1..nb-1); CTA 0 only coordinates.
 __device__ __forceinline__ int lf_row_start(int I, int nwk, int w) {
@@ -314,31 +327,37 @@ __device__ __forceinline__ int lf_row_start(int I, int nwk, int w) {
 // The workers add their keys with relaxed atomics and no fence or arrival
 // flag: the coarse bins are complete once they and the NaN count add up to I
 // (every count only grows towards its final value), and a coarse bin's fine
-// bins once they add up to its coarse count.  It clears the coarse histogram,
-// the NaN count and the count words it read; the workers clear the fine bins
-// they filled.
+// bins once they add up to its coarse count.  It clears the coarse histogram
+// and the NaN count; the workers clear the fine bins.
+//
+// Tensor parallel (TP): every rank's workers add their keys to every rank's
+// histograms (remote reductions over NVLink), so each rank's coordinator sees
+// the histogram of all I channels and computes the same selection.  The
+// prefix of release 2 runs over the workers of all ranks in rank order:
+// worker counts of lower ranks arrive as tagged words in cnt[q][*].
+template <bool TP>
 __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int I, int nb,
-                                           unsigned tag) {
+                                           unsigned tag, int rank, int par) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwk = nb - 1;
+  const unsigned* fine = sel->fine[par];
   __shared__ int s_cnt[2 * kLfMaxCtas];
   if (warp == 0) {
     int c8[8], loc = 0;
     bool ok = false;
-    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+    for (uint32_t it = 0, lim = spin_limit(err); it < lim && !ok; ++it) {
       // bins 255 - 8 lane - q, q = 0..7: the 8 words from 248 - 8 lane, reversed
-      const uint4 hi4 = ld_relaxed_v4(sel->coarse + 252 - 8 * lane);
-      const uint4 lo4 = ld_relaxed_v4(sel->coarse + 248 - 8 * lane);
+      const uint4 hi4 = lf_ld_v4<TP>(sel->coarse + 252 - 8 * lane);
+      const uint4 lo4 = lf_ld_v4<TP>(sel->coarse + 248 - 8 * lane);
       c8[0] = (int)hi4.w; c8[1] = (int)hi4.z; c8[2] = (int)hi4.y; c8[3] = (int)hi4.x;
       c8[4] = (int)lo4.w; c8[5] = (int)lo4.z; c8[6] = (int)lo4.y; c8[7] = (int)lo4.x;
       loc = 0;
 #pragma unroll
       for (int q = 0; q < 8; ++q) loc += c8[q];
-      const int nan = lane == 0 ? (int)ld_relaxed_u32(&sel->nan_count) : 0;
+      const int nan = lane == 0 ? (int)lf_ld_u32<TP>(&sel->nan_count) : 0;
       ok = __reduce_add_sync(0xffffffffu, loc + nan) == I;
     }
     if (!ok && lane == 0) atomicOr(err, kErrTimeout);
-    LF_CTA(13);
     int incl = loc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -375,12 +394,12 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
     int fb[4][4];
     const int fbin[4] = {b1 - 1, b1, b1 + 1, btop};
     ok = false;
-    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+    for (uint32_t it = 0, lim = spin_limit(err); it < lim && !ok; ++it) {
 #pragma unroll
       for (int d = 0; d < 4; ++d) {
         const int cb = fbin[d];
         const bool use = cb >= 0 && cb < 256 && (d == 3 || has_w);
-        const uint4 v = use ? ld_relaxed_v4(sel->fine + ((cb << 7) | (lane * 4)))
+        const uint4 v = use ? lf_ld_v4<TP>(fine + ((cb << 7) | (lane * 4)))
                             : make_uint4(0u, 0u, 0u, 0u);
         fb[d][0] = (int)v.x; fb[d][1] = (int)v.y; fb[d][2] = (int)v.z; fb[d][3] = (int)v.w;
       }
@@ -394,7 +413,6 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       }
     }
     if (!ok && lane == 0) atomicOr(err, kErrTimeout);
-    LF_CTA(15);
     int kmax = -1;
 #pragma unroll
     for (int q = 0; q < 4; ++q)
@@ -431,7 +449,6 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       hi = up ? hi : t;
       t = __fmul_rn(0.5f, __fadd_rn(lo, hi));
     }
-    LF_CTA(20);
     // #keys > tt = #keys >= kmin, kmin the bf16 key just above tt
     auto count_above = [&](float tt) -> int {
       const int kmin = (int)(__float_as_uint(tt) >> 16) + 1;
@@ -447,8 +464,8 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       } else {  // rare: a bin not loaded above, read until complete
         const int want = coarse_at(cb);
         bool okb = false;
-        for (uint32_t it = 0; it < kSpinLimit && !okb; ++it) {
-          const uint4 v = ld_relaxed_v4(sel->fine + ((cb << 7) | (lane * 4)));
+        for (uint32_t it = 0, lim = spin_limit(err); it < lim && !okb; ++it) {
+          const uint4 v = lf_ld_v4<TP>(fine + ((cb << 7) | (lane * 4)));
           fv[0] = (int)v.x; fv[1] = (int)v.y; fv[2] = (int)v.z; fv[3] = (int)v.w;
           okb = __reduce_add_sync(0xffffffffu, fv[0] + fv[1] + fv[2] + fv[3]) == want;
         }
@@ -461,7 +478,6 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       return __reduce_add_sync(0xffffffffu, part) + suffix_at(cb + 1);
     };
     const int totA = count_above(hi);
-    LF_CTA(23);
     const int above_lo = count_above(lo);
     // all keys are in: clear the coarse bins for the next call
     *reinterpret_cast<uint4*>(sel->coarse + 4 * lane) = make_uint4(0u, 0u, 0u, 0u);
@@ -473,23 +489,42 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       sel->par[lane] = lf_tagged(tag, v);
     }
   }
-  LF_CTA(14);
-  // round 2: every worker's (tier A, tier B) count word, prefix, release 2
+  // round 2: every worker's (tier A, tier B) count word (TP: of this rank
+  // and the lower ranks), prefix, release 2
+  __shared__ int s_low[2];
   for (int i = tid; i < 2 * kLfMaxCtas; i += kLfThreads) s_cnt[i] = 0;
+  if (tid < 2) s_low[tid] = 0;
   __syncthreads();
-  if (tid >= 1 && tid <= nwk) {
-    unsigned long long v = 0;
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {
-      asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(sel->cnt + tid) : "memory");
-      if (v >> 63) break;
+  {
+    int la = 0, lb = 0;
+    const int nent = (TP ? rank + 1 : 1) * nwk;
+    for (int e = tid; e < nent; e += kLfThreads) {
+      const int q = e / nwk, w = 1 + e - q * nwk;
+      const unsigned long long* p = &sel->cnt[q][w];
+      unsigned long long v = 0;
+      bool ok = false;
+      for (uint32_t it = 0, lim = spin_limit(err); it < lim && !ok; ++it) {
+        if (TP) v = ld_acquire_sys_u64(p);
+        else asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+        ok = (unsigned)(v >> 32) == tag;
+      }
+      if (!ok) { atomicOr(err, kErrTimeout); v = 0; }
+      const int ca = (int)((v >> 16) & 0xFFFFu), cb = (int)(v & 0xFFFFu);
+      if (TP && q < rank) {
+        la += ca;
+        lb += cb;
+      } else {
+        s_cnt[2 * (w - 1)] = ca;
+        s_cnt[2 * (w - 1) + 1] = cb;
+      }
     }
-    if (!(v >> 63)) { atomicOr(err, kErrTimeout); v = 0; }
-    sel->cnt[tid] = 0ull;
-    s_cnt[2 * (tid - 1)] = (int)((v >> 32) & 0x7FFFFFFF);
-    s_cnt[2 * (tid - 1) + 1] = (int)(v & 0xFFFFFFFFu);
+    if (TP && rank > 0) {
+      la = __reduce_add_sync(0xffffffffu, la);
+      lb = __reduce_add_sync(0xffffffffu, lb);
+      if (lane == 0 && (la | lb)) { atomicAdd(&s_low[0], la); atomicAdd(&s_low[1], lb); }
+    }
   }
   __syncthreads();
-  LF_CTA(21);
   if (warp == 0) {
     int va[5], vb[5], la = 0, lb = 0;
 #pragma unroll
@@ -506,7 +541,7 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       const int ta = __shfl_up_sync(0xffffffffu, ia, o), tb = __shfl_up_sync(0xffffffffu, ib, o);
       if (lane >= o) { ia += ta; ib += tb; }
     }
-    int pa = ia - la, pb = ib - lb;
+    int pa = ia - la + s_low[0], pb = ib - lb + s_low[1];
 #pragma unroll
     for (int q = 0; q < 5; ++q) {  // release 2
       const int c = lane * 5 + q;
@@ -518,24 +553,38 @@ __device__ __noinline__ void lf_coordinate(unsigned* err, LfSel* sel, int K, int
       pb += vb[q];
     }
   }
-  LF_CTA(22);
 }
 
-template <int GW, bool CA>
+template <int GW, bool CA, bool TP>
 __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs a) {
   using Geo = LfGeom<GW>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  const int H = a.hidden, I = a.inter, K = a.k;
+  // I: this GPU's rows; IT: all channels (equal unless TP)
+  const int H = a.hidden, I = a.inter, K = a.k, IT = TP ? a.inter_total : a.inter;
   const int rowb = H / 2, scw = H / kGroup;  // bytes per packed row, scales per row
   const int nb = gridDim.x, b = blockIdx.x, nwk = nb - 1;
+  const int rank = TP ? a.rank : 0;
   LfSel* sel = reinterpret_cast<LfSel*>(a.scratch);
-  LF_CTA(0);
+  // this call's tag (from the final barrier's counter, which grows by the
+  // grid size once per call) and, TP, the parity of the call index (which
+  // fine histogram set the call uses)
+  __shared__ unsigned s_tag;
+  __shared__ int s_cpar;
+  auto read_tag = [&]() {
+    if (tid == 0) {
+      const unsigned long long d0 = ld_cg_u64(&sel->done);
+      s_tag = lf_tag(d0);
+      s_cpar = TP ? (int)((d0 / (unsigned long long)nb) & 1ull) : 0;
+    }
+  };
 
   if (b == 0) {
     pdl_wait();
-    lf_coordinate(a.err, sel, K, I, nb, lf_tag(ld_cg_u64(&sel->done)));
+    read_tag();
+    __syncthreads();
+    lf_coordinate<TP>(a.err, sel, K, IT, nb, s_tag, rank, s_cpar);
   } else {
   uint8_t* ring = smem + warp * kLfDepth * Geo::slot;
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Geo::xs);
@@ -546,8 +595,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // GW == 1 reads the scale of group `warp` from the 4-byte word copied at
   // (warp & ~1); GW == 2 reads both halves.
   const int sc_sel = (GW == 1) ? (warp & 1) : 0;
-  // this call's tag (from the final barrier's counter, which grows once per call)
-  __shared__ unsigned s_tag;
 
   // ------------------------------------------------------------ phase A
   const int ra0 = lf_row_start(I, nwk, b - 1), ra1 = lf_row_start(I, nwk, b);
@@ -566,10 +613,8 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // queue behind every line this SM has requested, so the other tiles are
   // requested right after them.
   issue_a(0);
-  LF_TRACE(0);
   pdl_wait();
-  if (tid == 0) s_tag = lf_tag(ld_cg_u64(&sel->done));
-  LF_TRACE(1);
+  read_tag();
 
   // Layer input: x, or RMSNorm(x + resid); one 16-byte word (8 values) per
   // thread (H / 8 <= kLfThreads, checked on the host), staged in the
@@ -640,7 +685,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     if ((lane & 15) == 0 && mine) gsum[tid >> 4] = part;
   }
   __syncthreads();
-  LF_TRACE(2);
   uint32_t xf[GW][16];
   float bias[GW];
 #pragma unroll
@@ -659,8 +703,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     issue_a(i + kLfDepth - 1);
     cp_wait_lf();
     __syncwarp();
-    LF_TILE(i);
-    if (i == 0) LF_CTA(19);
     float pa, pb;
     lf_tile_dot<GW>(ring + (i % kLfDepth) * Geo::slot, xf, bias, lane, sc_sel, pa, pb);
     if (tq == 0) {
@@ -670,8 +712,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     __syncwarp();
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
-  LF_TRACE(3);
-  LF_CTA(1);
   __syncthreads();
   for (int r = tid; r < na; r += kLfThreads) {
     const int i = r >> 4, row = r & 15;
@@ -723,7 +763,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       if (r < na) cpos[r] = -1;
     }
     nv = __reduce_add_sync(0xffffffffu, nv);
-    const int nts_w = min(na * K / I / 16, nv / 16);  // na * K < 2^31 (host check)
+    const int nts_w = min(na * K / IT / 16, nv / 16);  // na * K < 2^31 (host check)
     if (nts_w > 0) {
       const int nspec = nts_w * 16;
       unsigned T = 0;
@@ -774,7 +814,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   }
   __syncthreads();
   const int nts = s_nts;
-  LF_CTA(3);
 
   // ------------------------------------------------------------ phases C + D
   // One cp.async stream per warp: spec up tiles, rest up tiles (this CTA's
@@ -855,12 +894,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // bins it filled, queue the up rows of its tier A rows and tie candidates
   // not speculated on, and list its tier A rows for the down projection.
   auto poll1 = [&]() {
-    LF_CTA(6);
     if (tid == 0) {
       const unsigned tag = s_tag;
       unsigned long long p[4];
       bool done = false;
-      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+      for (uint32_t it = 0, lim = spin_limit(a.err); it < lim && !done; ++it) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) p[q] = ld_relaxed_u64(sel->par + q);
         done = (unsigned)(p[0] >> 32) == tag && (unsigned)(p[1] >> 32) == tag &&
@@ -875,20 +913,40 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     __syncthreads();
   };
   auto apply1 = [&]() {
-    LF_CTA(8);
     const float lo = s_lohi[0], hi = s_lohi[1];
     isA = kv > hi;
     isB = kv > lo && kv <= hi;
     offAB = block_excl_scan2(isA, isB, warp_tot, totAB);
-    if (my_valid) sel->fine[my_key] = 0u;  // the coordinator has read the fine bins
-    if (tid == 0) {
-      const unsigned long long word =
-          (1ull << 63) | ((unsigned long long)totAB.x << 32) | (unsigned)totAB.y;
-      // the word is its own payload: a relaxed store suffices
-      asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(sel->cnt + b), "l"(word) : "memory");
+    if (!TP) {
+      if (my_valid) sel->fine[0][my_key] = 0u;  // the coordinator has read the fine bins
+    } else {
+      // Keys of every rank land in every rank's histogram, and a remote fine
+      // bin increment may still be in flight after the coordinator has read
+      // the bins it needs.  So a call clears the other set, which the
+      // previous call used: every increment of the previous call was issued
+      // before its rank sent its y slots of that call, which this rank
+      // received before this call.  The next call, which uses that set,
+      // starts its increments only after receiving this rank's y slots of
+      // this call, sent after this clear.
+      uint4* f4 = reinterpret_cast<uint4*>(sel->fine[s_cpar ^ 1]);
+      const int n4 = kTopkHistBins / 4;
+      for (int i = n4 * (b - 1) / nwk + tid; i < n4 * b / nwk; i += kLfThreads)
+        f4[i] = make_uint4(0u, 0u, 0u, 0u);
     }
-    // the owner of row 0 may need channel 0 for the index padding
-    const bool pad_maybe = b == 1 && s_par[1] < K;
+    if (tid == 0) {
+      // tagged word, its own payload: a relaxed store suffices.  TP: to this
+      // rank and every higher rank (their prefixes count this rank's rows).
+      const unsigned long long word = ((unsigned long long)s_tag << 32) |
+                                      ((unsigned)totAB.x << 16) | (unsigned)totAB.y;
+      if (TP) {
+        for (int q = rank; q < a.world; ++q) st_relaxed_sys_u64(&a.psel[q]->cnt[rank][b], word);
+      } else {
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(&sel->cnt[0][b]), "l"(word)
+                     : "memory");
+      }
+    }
+    // the owner of channel 0 may need it for the index padding
+    const bool pad_maybe = b == 1 && rank == 0 && s_par[1] < K;
     const bool restr = tid < na && (isA || isB || (pad_maybe && tid == 0)) && cpos[tid] < 0;
     int2 t2;
     const int2 o2 = block_excl_scan2(restr, false, warp_tot, t2);
@@ -913,12 +971,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // Release 2: this CTA's prefix counts.  Write its part of idx, append the
   // selected tie rows and the padding entry to the down list.
   auto poll2 = [&]() {
-    LF_CTA(7);
     if (tid == 0) {
       const unsigned tag = s_tag;
       unsigned long long p0 = 0, p1 = 0;
       bool done = false;
-      for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+      for (uint32_t it = 0, lim = spin_limit(a.err); it < lim && !done; ++it) {
         p0 = ld_relaxed_u64(&sel->pre[b][0]);
         p1 = ld_relaxed_u64(&sel->pre[b][1]);
         done = (unsigned)(p0 >> 32) == tag && (unsigned)(p1 >> 32) == tag;
@@ -930,13 +987,13 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     __syncthreads();
   };
   auto apply2 = [&]() {
-    LF_CTA(9);
     const int totA = s_par[0], filled = s_par[1], selB = filled - totA;
     const int preA = s_par[2], preB = s_par[3];
     const int nB = max(0, min(totAB.y, selB - preB));
-    if (isA && preA + offAB.x < K) a.idx[preA + offAB.x] = ra0 + tid;
+    const int c0 = TP ? a.c0 : 0;  // channel id of this GPU's row 0
+    if (isA && preA + offAB.x < K && a.idx) a.idx[preA + offAB.x] = c0 + ra0 + tid;
     if (isB && offAB.y < nB) {
-      a.idx[totA + preB + offAB.y] = ra0 + tid;
+      if (a.idx) a.idx[totA + preB + offAB.y] = c0 + ra0 + tid;
       drow[nDA + offAB.y] = ra0 + tid;
       dsrc[nDA + offAB.y] = cpos[tid];
       dh[nDA + offAB.y] = bf16_bits_to_f32(gloc[tid]);
@@ -944,11 +1001,12 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     {
       const int per = (K - filled + nwk - 1) / nwk;
       const int z0 = filled + (b - 1) * per, z1 = min(K, z0 + per);
-      for (int i2 = z0 + tid; i2 < z1; i2 += kLfThreads) a.idx[i2] = 0;
+      if (rank == 0 && a.idx)
+        for (int i2 = z0 + tid; i2 < z1; i2 += kLfThreads) a.idx[i2] = 0;
     }
     // The K - filled zero indices select channel 0 that many times: the
     // owner of row 0 adds one down entry for it, h scaled by the count.
-    const bool pad = b == 1 && filled < K;
+    const bool pad = b == 1 && rank == 0 && filled < K;
     const int nd = nDA + nB + (pad ? 1 : 0);
     if (tid == 0) {
       if (pad) {
@@ -981,22 +1039,37 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // This CTA's part of the global histograms: one relaxed atomic per distinct
   // key and coarse bin, no fence and no arrival flag (the coordinator checks
   // the totals), then the stream goes on at once.
+  // TP: the same increments go to every rank's histograms over NVLink.
   if (tid < 256) {
     const unsigned kk = hkey[tid];
-    if (kk != 0xFFFFFFFFu) atomicAdd(&sel->fine[kk], hcnt[tid]);
+    if (kk != 0xFFFFFFFFu) {
+      if (TP) {
+        for (int q = 0; q < a.world; ++q) red_add_sys(&a.psel[q]->fine[s_cpar][kk], hcnt[tid]);
+      } else {
+        atomicAdd(&sel->fine[0][kk], hcnt[tid]);
+      }
+    }
   } else if (tid < 512) {
     const unsigned c = hcrs[tid - 256];
-    if (c) atomicAdd(&sel->coarse[tid - 256], c);
+    if (c) {
+      if (TP) {
+        for (int q = 0; q < a.world; ++q) red_add_sys(&a.psel[q]->coarse[tid - 256], c);
+      } else {
+        atomicAdd(&sel->coarse[tid - 256], c);
+      }
+    }
   } else if (tid == 512 && s_nnan) {
-    atomicAdd(&sel->nan_count, s_nnan);
+    if (TP) {
+      for (int q = 0; q < a.world; ++q) red_add_sys(&a.psel[q]->nan_count, s_nnan);
+    } else {
+      atomicAdd(&sel->nan_count, s_nnan);
+    }
   }
-  LF_CTA(2);
 #pragma unroll 1
   for (int j = 0; j < kLfDepth - 1; ++j) { need(j); issue(j); }
   for (int j = 0; j < nC; ++j) {
     cp_wait_lf2();
     __syncwarp();
-    LF_TILE(16 + j);
     need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
     float pa, pb;
@@ -1011,8 +1084,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   __syncthreads();
   make_h(0, have2 ? nD * 16 : nDA);
   c_done = true;
-  LF_TRACE(7);
-  LF_CTA(10);
   float acc[GW][8][4];
 #pragma unroll
   for (int u = 0; u < GW; ++u)
@@ -1026,10 +1097,8 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   for (int j = nC; j < nC + nD; ++j) {
     cp_wait_lf2();
     __syncwarp();
-    LF_TILE(16 + j);
     need(j + kLfDepth - 1);
     issue(j + kLfDepth - 1);
-    if (j == nC) LF_CTA(17);
     const uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
     const int i = j - nC;
     uint32_t bval = 0;
@@ -1075,8 +1144,6 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     __syncwarp();
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
-  LF_TRACE(9);
-  LF_CTA(4);
 #pragma unroll
   for (int u = 0; u < GW; ++u) {
     float cs = colsum;
@@ -1096,13 +1163,9 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
   }
-  LF_TRACE(10);
-  LF_CTA(5);
   }  // worker
   pdl_launch_dependents();
   lf_final_barrier(&sel->done, a.err);
-  LF_TRACE(11);
-  LF_CTA(11);
 
   // ------------------------------------------------------------ phase E
   // y[4q .. 4q+3] for this CTA's quads (at most 10): two warps per quad, lane
@@ -1139,10 +1202,50 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     float4* e4 = reinterpret_cast<float4*>(red);
     if (lane == 0 && (warp & 1)) e4[q] = s4;
     __syncthreads();
-    LF_CTA(18);
-    if (lane == 0 && !(warp & 1) && q < nq) {
+    const bool owner = lane == 0 && !(warp & 1) && q < nq;
+    if (owner) {
       const float4 o4 = e4[q];
       s4.x += o4.x; s4.y += o4.y; s4.z += o4.z; s4.w += o4.w;
+    }
+    if (TP) {
+      // This rank's partial sums of the CTA's quads go to slot `rank` of
+      // every rank's y slots (plain 16-byte stores over NVLink), then one
+      // tagged flag per rank; CTA b of every rank owns the same quads, so it
+      // waits for the flags of CTA b of every rank and sums the slots in rank
+      // order: y is identical on every rank.
+      const int o = 4 * (q0 + q);
+      if (owner)
+        for (int r = 0; r < a.world; ++r)
+          *reinterpret_cast<float4*>(a.pysl[r] + (size_t)rank * H + o) = s4;
+      __syncthreads();
+      if (tid == 0) {
+        const unsigned long long tag = s_tag;
+        asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+        for (int r = 0; r < a.world; ++r)
+          st_relaxed_sys_u64(a.pyflag[r] + (size_t)rank * kLfMaxCtas + b, tag);
+        const unsigned long long* mine = a.pyflag[rank];
+        bool ok = true;
+        for (int r = 0; r < a.world && ok; ++r) {
+          ok = false;
+          for (uint32_t it = 0, lim = spin_limit(a.err); it < lim && !ok; ++it)
+            ok = ld_acquire_sys_u64(mine + (size_t)r * kLfMaxCtas + b) == tag;
+        }
+        if (!ok) atomicOr(a.err, kErrTimeout);
+      }
+      __syncthreads();
+      if (owner) {
+        const float* ys = a.pysl[rank];
+        s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < a.world; ++r) {
+          float4 v;
+          asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                       : "l"(ys + (size_t)r * H + o) : "memory");
+          s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+        }
+      }
+    }
+    if (owner) {
       const int o = 4 * (q0 + q);
       if (a.y) {
         a.y[o] = f32_to_bf16_bits(s4.x); a.y[o + 1] = f32_to_bf16_bits(s4.y);
@@ -1151,30 +1254,87 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       if (a.y_f32) *reinterpret_cast<float4*>(a.y_f32 + o) = s4;
     }
   }
-  LF_TRACE(12);
-  LF_CTA(12);
 }
 
 constexpr size_t kLfSelBytes = (sizeof(LfSel) + 255) & ~size_t(255);
 
-size_t layer_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
-  const size_t s = kLfSelBytes + 256 +
-                   (((size_t)inter * 2 + 255) & ~size_t(255)) + (((size_t)k * 4 + 255) & ~size_t(255)) +
-                   (size_t)num_sms() * hidden * 4;
-  return s;
+// Workspace layout (byte offsets).  The single-GPU workspace is the prefix up
+// to `ysl`; the tensor-parallel one adds the y slots and y flags that the
+// peers write into.
+struct LfLayout {
+  size_t bar, g, idx, part, ysl, yflag, single_total, tp_total;
+};
+static size_t lf_al(size_t v) { return (v + 255) & ~size_t(255); }
+static LfLayout lf_layout(int64_t hidden, int64_t inter, int64_t k) {
+  LfLayout L;
+  L.bar = kLfSelBytes;
+  L.g = L.bar + 256;
+  L.idx = L.g + lf_al((size_t)inter * 2);
+  L.part = L.idx + lf_al((size_t)k * 4);
+  L.ysl = L.part + (size_t)kLfMaxCtas * hidden * 4;  // device independent: up to 160 SMs
+  L.single_total = L.ysl;
+  L.yflag = L.ysl + lf_al((size_t)kLfMaxRanks * hidden * 4);
+  L.tp_total = L.yflag + lf_al((size_t)kLfMaxRanks * kLfMaxCtas * 8);
+  return L;
 }
 
 }  // namespace dip
 
 namespace dip {
-template <int GW, bool CA>
+template <int GW, bool CA, bool TP>
 static int lf_launch(const LfArgs& a, int nb, dip_stream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(layer_fused_kernel<GW, CA>,
+  cudaError_t e = cudaFuncSetAttribute(layer_fused_kernel<GW, CA, TP>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        LfGeom<GW>::total);
   if (e != cudaSuccess) return launch_status(e);
-  return launch_status(launch_coop(layer_fused_kernel<GW, CA>, dim3(nb), dim3(kLfThreads),
+  return launch_status(launch_coop(layer_fused_kernel<GW, CA, TP>, dim3(nb), dim3(kLfThreads),
                                    (size_t)LfGeom<GW>::total, (cudaStream_t)stream, a));
+}
+
+// Shape checks shared by the entry points; returns 0 and the K-slice width
+// (GW) or a status.  I: rows on this GPU, IT: all channels.
+static int lf_check_shape(int64_t H, int64_t I, int64_t IT, int64_t k, int nb, int* gw_out) {
+  if (k < 1 || k > IT || H <= 0 || I <= 0) return DIP_ERR_ARG;
+  if (nb > kLfMaxCtas) return DIP_ERR_UNSUPPORTED;
+  const int G = (int)(H / kGroup);
+  int gw = 0;
+  if (H % kGroup == 0 && G == kLfWarps * 1) gw = 1;
+  if (H % kGroup == 0 && G == kLfWarps * 2) gw = 2;
+  if (!gw || I % 8 != 0) return DIP_ERR_UNSUPPORTED;
+  // per-worker limits (CTA 0 coordinates): gate rows <= 16*kLfTilesA - 1
+  // (C list: rows plus one padding entry, in at most kLfTilesA + 1 tiles)
+  if (nb < 2 || (I + nb - 2) / (nb - 1) > 16 * kLfTilesA - 1 || IT * (int64_t)nb >= (int64_t(1) << 31) ||
+      (H / 4 + nb - 1) / nb > kLfWarps / 2 ||
+      (int64_t)16 * kLfTilesA * k >= (int64_t(1) << 31))
+    return DIP_ERR_UNSUPPORTED;
+  *gw_out = gw;
+  return DIP_OK;
+}
+
+static void lf_fill_common(LfArgs& a, const dip_layer_t* L, uint8_t* ws, const LfLayout& lay,
+                           const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
+                           dip_bf16* y, dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used) {
+  a.scratch = reinterpret_cast<unsigned*>(ws);
+  a.bar = reinterpret_cast<GridBar*>(ws + lay.bar);
+  a.g = g_out ? g_out : reinterpret_cast<uint16_t*>(ws + lay.g);
+  a.idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + lay.idx);
+  a.partial = reinterpret_cast<float*>(ws + lay.part);
+  a.gate_qw = reinterpret_cast<const uint8_t*>(L->gate_qw);
+  a.gate_sc = L->gate_sc;
+  a.up_qw = reinterpret_cast<const uint8_t*>(L->up_qw);
+  a.up_sc = L->up_sc;
+  a.dn_qw = reinterpret_cast<const uint8_t*>(L->down_t_qw);
+  a.dn_sc = L->down_t_sc;
+  a.hidden = (int)L->hidden;
+  a.inter = (int)L->inter;
+  a.inter_total = (int)L->inter;
+  a.world = 1;
+  a.k = (int)k;
+  a.x = x;
+  a.resid = resid;
+  a.eps = eps;
+  a.x_used = x_used;
+  a.y = y;
 }
 }  // namespace dip
 
@@ -1182,10 +1342,12 @@ using namespace dip;
 
 extern "C" size_t dip_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   if (hidden <= 0 || inter <= 0 || k <= 0) return 0;
-  // device independent upper bound (up to 160 SMs)
-  return kLfSelBytes + 256 +
-         (((size_t)inter * 2 + 255) & ~size_t(255)) + (((size_t)k * 4 + 255) & ~size_t(255)) +
-         (size_t)160 * hidden * 4;
+  return lf_layout(hidden, inter, k).single_total;
+}
+
+extern "C" size_t dip_mlp_fused_tp_workspace_bytes(int64_t hidden, int64_t inter_total, int64_t k) {
+  if (hidden <= 0 || inter_total <= 0 || k <= 0) return 0;
+  return lf_layout(hidden, inter_total, k).tp_total;
 }
 
 extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, const dip_bf16* resid,
@@ -1194,6 +1356,53 @@ extern "C" int dip_mlp_decode_fused(const dip_layer_t* L, const dip_bf16* x, con
                                     dip_bf16* x_used, dip_stream_t stream) {
   return dip_mlp_decode_fused_ca(L, nullptr, x, resid, eps, k, workspace, workspace_bytes, y, g_out,
                                  idx_out, x_used, stream);
+}
+
+extern "C" int dip_mlp_decode_fused_tp(const dip_layer_t* shard, int64_t inter_total, int rank,
+                                       int world, void* const* workspaces, size_t workspace_bytes,
+                                       const dip_bf16* x, const dip_bf16* resid, float eps,
+                                       int64_t k, dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
+                                       dip_bf16* x_used, dip_stream_t stream) {
+  if (!shard || !x || !y || !workspaces) return DIP_ERR_ARG;
+  if (world < 1 || world > kLfMaxRanks || rank < 0 || rank >= world) return DIP_ERR_ARG;
+  const int64_t H = shard->hidden, I = shard->inter;
+  if (I <= 0 || inter_total != I * world) return DIP_ERR_ARG;
+  const int nb = num_sms();
+  int gw = 0;
+  const int st = lf_check_shape(H, I, inter_total, k, nb, &gw);
+  if (st) return st;
+  const LfLayout lay = lf_layout(H, inter_total, k);
+  if (workspace_bytes < lay.tp_total) return DIP_ERR_WORKSPACE;
+  for (int q = 0; q < world; ++q) {
+    if (!workspaces[q] || (reinterpret_cast<uintptr_t>(workspaces[q]) & 255)) return DIP_ERR_ARG;
+    // a peer's workspace is another GPU's memory: it must be a mapping this
+    // library opened (dip_ipc_open) or allocated, of at least the layout's
+    // size, or the peer stores below would land outside it
+    if (q != rank && p2p_registered_bytes(workspaces[q]) < lay.tp_total) return DIP_ERR_ARG;
+  }
+  const uintptr_t al = reinterpret_cast<uintptr_t>(shard->gate_qw) |
+                       reinterpret_cast<uintptr_t>(shard->up_qw) |
+                       reinterpret_cast<uintptr_t>(shard->down_t_qw) | reinterpret_cast<uintptr_t>(x) |
+                       reinterpret_cast<uintptr_t>(resid) | reinterpret_cast<uintptr_t>(x_used) |
+                       reinterpret_cast<uintptr_t>(g_out);
+  if (al & 15) return DIP_ERR_ARG;
+  LfArgs a = {};
+  uint8_t* ws = static_cast<uint8_t*>(workspaces[rank]);
+  lf_fill_common(a, shard, ws, lay, x, resid, eps, k, y, g_out, idx_out, x_used);
+  a.idx = idx_out;  // optional: only this rank's entries are written
+  a.inter_total = (int)inter_total;
+  a.rank = rank;
+  a.world = world;
+  a.c0 = (int)(I * rank);
+  for (int q = 0; q < world; ++q) {
+    uint8_t* wq = static_cast<uint8_t*>(workspaces[q]);
+    a.psel[q] = reinterpret_cast<LfSel*>(wq);
+    a.pysl[q] = reinterpret_cast<float*>(wq + lay.ysl);
+    a.pyflag[q] = reinterpret_cast<unsigned long long*>(wq + lay.yflag);
+  }
+  a.err = error_word_ptr();
+  if (!a.err) return DIP_ERR_CUDA;
+  return gw == 1 ? lf_launch<1, false, true>(a, nb, stream) : lf_launch<2, false, true>(a, nb, stream);
 }
 
 extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_t* cache,
@@ -1209,51 +1418,20 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
                  reinterpret_cast<uintptr_t>(cache->res_dn_qw)) & 15))
     return DIP_ERR_ARG;
   const int64_t H = L->hidden, I = L->inter;
-  if (k < 1 || k > I || H <= 0 || I <= 0) return DIP_ERR_ARG;
   const int nb = num_sms();
-  if (nb > 160) return DIP_ERR_UNSUPPORTED;
-  const int G = (int)(H / kGroup);
   int gw = 0;
-  if (H % kGroup == 0 && G == kLfWarps * 1) gw = 1;
-  if (H % kGroup == 0 && G == kLfWarps * 2) gw = 2;
-  if (!gw || I % 8 != 0) return DIP_ERR_UNSUPPORTED;
-  // per-worker limits (CTA 0 coordinates): gate rows <= 16*kLfTilesA - 1
-  // (C list: rows plus one padding entry, in at most kLfTilesA + 1 tiles)
-  if (nb < 2 || (I + nb - 2) / (nb - 1) > 16 * kLfTilesA - 1 || I * (int64_t)nb >= (int64_t(1) << 31) ||
-      (H / 4 + nb - 1) / nb > kLfWarps / 2 ||
-      (int64_t)16 * kLfTilesA * k >= (int64_t(1) << 31))
-    return DIP_ERR_UNSUPPORTED;
-  if (workspace_bytes < dip_mlp_fused_workspace_bytes(H, I, k)) return DIP_ERR_WORKSPACE;
+  const int st = lf_check_shape(H, I, I, k, nb, &gw);
+  if (st) return st;
+  const LfLayout lay = lf_layout(H, I, k);
+  if (workspace_bytes < lay.single_total) return DIP_ERR_WORKSPACE;
   const uintptr_t al = reinterpret_cast<uintptr_t>(L->gate_qw) | reinterpret_cast<uintptr_t>(L->up_qw) |
                        reinterpret_cast<uintptr_t>(L->down_t_qw) | reinterpret_cast<uintptr_t>(x) |
                        reinterpret_cast<uintptr_t>(resid) | reinterpret_cast<uintptr_t>(x_used) |
                        reinterpret_cast<uintptr_t>(g_out) | reinterpret_cast<uintptr_t>(workspace);
   if (al & 15) return DIP_ERR_ARG;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
   LfArgs a = {};
-  a.scratch = reinterpret_cast<unsigned*>(ws);
-  ws += kLfSelBytes;
-  a.bar = reinterpret_cast<GridBar*>(ws);
-  ws += 256;
-  a.g = g_out ? g_out : reinterpret_cast<uint16_t*>(ws);
-  ws += ((size_t)I * 2 + 255) & ~size_t(255);
-  a.idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws);
-  ws += ((size_t)k * 4 + 255) & ~size_t(255);
-  a.partial = reinterpret_cast<float*>(ws);
-  a.gate_qw = reinterpret_cast<const uint8_t*>(L->gate_qw);
-  a.gate_sc = L->gate_sc;
-  a.up_qw = reinterpret_cast<const uint8_t*>(L->up_qw);
-  a.up_sc = L->up_sc;
-  a.dn_qw = reinterpret_cast<const uint8_t*>(L->down_t_qw);
-  a.dn_sc = L->down_t_sc;
-  a.hidden = (int)H;
-  a.inter = (int)I;
-  a.k = (int)k;
-  a.x = x;
-  a.resid = resid;
-  a.eps = eps;
-  a.x_used = x_used;
-  a.y = y;
+  lf_fill_common(a, L, static_cast<uint8_t*>(workspace), lay, x, resid, eps, k, y, g_out, idx_out,
+                 x_used);
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
   if (cache) {
@@ -1264,6 +1442,7 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
     a.res_dn_sc = cache->res_dn_sc;
   }
   const bool ca = cache != nullptr;
-  if (gw == 1) return ca ? lf_launch<1, true>(a, nb, stream) : lf_launch<1, false>(a, nb, stream);
-  return ca ? lf_launch<2, true>(a, nb, stream) : lf_launch<2, false>(a, nb, stream);
+  if (gw == 1)
+    return ca ? lf_launch<1, true, false>(a, nb, stream) : lf_launch<1, false, false>(a, nb, stream);
+  return ca ? lf_launch<2, true, false>(a, nb, stream) : lf_launch<2, false, false>(a, nb, stream);
 }

@@ -21,10 +21,57 @@
 // the partial slots.  Waits are bounded: on timeout the library's error word
 // is flagged and the kernel returns.
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "dip_common.cuh"
 
 namespace dip {
+
+// Host-side record of the device ranges this library allocated for peer
+// exchange or mapped from a peer: base -> size.
+static std::mutex g_reg_mu;
+static std::map<uintptr_t, size_t> g_reg;
+
+static void reg_add(const void* base, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  g_reg[reinterpret_cast<uintptr_t>(base)] = bytes;
+}
+static void reg_del(const void* base) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  g_reg.erase(reinterpret_cast<uintptr_t>(base));
+}
+size_t p2p_registered_bytes(const void* p) {
+  const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.upper_bound(v);
+  if (it == g_reg.begin()) return 0;
+  --it;
+  const uintptr_t end = it->first + it->second;
+  return v < end ? (size_t)(end - v) : 0;
+}
+
+// Size of the allocation an IPC mapping covers, from the driver
+// (cuMemGetAddressRange, fetched through the runtime's entry-point query so
+// the library needs no link against libcuda).
+static size_t mapped_range_bytes(void* ptr) {
+  using Fn = int (*)(unsigned long long*, size_t*, unsigned long long);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(f);
+  });
+  if (!fn) return 0;
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0) return 0;
+  const unsigned long long v = reinterpret_cast<unsigned long long>(ptr);
+  return v >= base && v < base + size ? (size_t)(base + size - v) : 0;
+}
 
 constexpr int kP2PMaxRanks = 8;
 constexpr size_t kP2PHeader = 512;
@@ -96,7 +143,7 @@ __global__ void __launch_bounds__(1024) p2p_exchange_kernel(const P2PArgs a, int
     st_release_sys(p2p_flags(a.mb[tid]) + which * kP2PMaxRanks + a.rank, epoch + 1);
     const unsigned long long* f = p2p_flags(mine) + which * kP2PMaxRanks + tid;
     bool ok = false;
-    for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) ok = ld_acquire_sys(f) >= epoch + 1;
+    for (uint32_t it = 0, lim = spin_limit(a.err); it < lim && !ok; ++it) ok = ld_acquire_sys(f) >= epoch + 1;
     if (!ok) atomicOr(a.err, kErrTimeout);
   }
   __syncthreads();
@@ -125,10 +172,16 @@ extern "C" int dip_p2p_alloc(size_t bytes, void** ptr) {
   if (!ptr || bytes == 0) return DIP_ERR_ARG;
   cudaError_t e = cudaMalloc(ptr, bytes);
   if (e != cudaSuccess) return launch_status(e);
-  return launch_status(cudaMemset(*ptr, 0, bytes));
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return launch_status(e);
+  reg_add(*ptr, bytes);
+  return DIP_OK;
 }
 
-extern "C" int dip_p2p_free(void* ptr) { return launch_status(cudaFree(ptr)); }
+extern "C" int dip_p2p_free(void* ptr) {
+  reg_del(ptr);
+  return launch_status(cudaFree(ptr));
+}
 
 extern "C" int dip_ipc_handle(const void* ptr, void* handle64) {
   if (!ptr || !handle64) return DIP_ERR_ARG;
@@ -144,20 +197,37 @@ extern "C" int dip_ipc_open(const void* handle64, void** ptr) {
   if (!handle64 || !ptr) return DIP_ERR_ARG;
   cudaIpcMemHandle_t h;
   memcpy(&h, handle64, sizeof(h));
-  return launch_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  const int st = launch_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  if (st != DIP_OK) return st;
+  const size_t n = mapped_range_bytes(*ptr);
+  if (n == 0) {
+    cudaIpcCloseMemHandle(*ptr);
+    *ptr = nullptr;
+    return DIP_ERR_CUDA;
+  }
+  reg_add(*ptr, n);
+  return DIP_OK;
 }
 
-extern "C" int dip_ipc_close(void* ptr) { return launch_status(cudaIpcCloseMemHandle(ptr)); }
+extern "C" int dip_ipc_close(void* ptr) {
+  reg_del(ptr);
+  return launch_status(cudaIpcCloseMemHandle(ptr));
+}
 
 static int p2p_launch(int which, int rank, int world, void* const* mailboxes, int64_t n_local,
                       int64_t inter, int64_t hidden, const dip_bf16* g_local, const float* partial,
                       dip_bf16* y, dip_stream_t stream) {
   if (world < 1 || world > kP2PMaxRanks || rank < 0 || rank >= world || !mailboxes) return DIP_ERR_ARG;
+  if (inter <= 0 || hidden <= 0 || inter % world || n_local != inter / world) return DIP_ERR_ARG;
+  const size_t need = dip_p2p_mailbox_bytes(inter, hidden, world);
   P2PArgs a = {};
   a.rank = rank;
   a.world = world;
   for (int q = 0; q < world; ++q) {
     if (!mailboxes[q] || (reinterpret_cast<uintptr_t>(mailboxes[q]) & 255)) return DIP_ERR_ARG;
+    // every mailbox receives stores from this kernel: each must be a range
+    // this library allocated or mapped, large enough for this shape
+    if (p2p_registered_bytes(mailboxes[q]) < need) return DIP_ERR_ARG;
     a.mb[q] = static_cast<uint8_t*>(mailboxes[q]);
   }
   a.n_local = n_local;

@@ -23,15 +23,6 @@ namespace dip {
 
 constexpr int kTopkThreads = 1024;
 
-// Phase tracing (compile with -DDIP_TRACE): thread 0 of block 0 records the
-// SM clock at numbered points into dip_trace_clock[].
-#ifdef DIP_TRACE
-__device__ long long dip_trace_clock[16];
-#define DIP_TRACE_POINT(n) \
-  do { if (threadIdx.x == 0 && blockIdx.x == 0) dip_trace_clock[n] = clock64(); } while (0)
-#else
-#define DIP_TRACE_POINT(n) do { } while (0)
-#endif
 constexpr int kTopkMaxN = 98304;  // keys kept in shared memory (2 B each)
 constexpr uint16_t kNanKey = 0xFFFF;  // as a float pattern (<<16) this is a NaN
 
@@ -419,7 +410,7 @@ topk_compact_kernel(const uint16_t* __restrict__ s, int n, int k, int32_t* __res
     int pa = 0, pb = 0;
     for (int c = lane; c < (int)blockIdx.x; c += 32) {
       unsigned long long v = 0;
-      for (uint32_t it = 0; it < kSpinLimit; ++it) {
+      for (uint32_t it = 0, lim = spin_limit(err); it < lim; ++it) {
         asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(status + c) : "memory");
         if (v >> 63) break;
       }

@@ -16,6 +16,10 @@
 #include <ATen/ATen.h>
 #include <torch/library.h>
 
+#include <map>
+#include <mutex>
+#include <vector>
+
 #include "../../include/dip_b200.h"
 
 namespace {
@@ -60,6 +64,28 @@ Tensor bf16_empty(int64_t n, const Tensor& like) {
   return at::empty({n}, like.options().dtype(at::kBFloat16));
 }
 
+// The histogram of dip_topk_select_ws must be zero on entry and is left
+// zero, so one buffer per (device, stream) serves every call issued on that
+// stream: it is allocated and zeroed once.  While the stream is being
+// captured into a CUDA graph a fresh zeroed buffer is used instead (a buffer
+// first zeroed inside a capture would only be zeroed at replay).
+Tensor topk_hist_for(const Tensor& like) {
+  const int64_t nb = (int64_t)dip_topk_hist_bytes();
+  cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return at::zeros({nb}, like.options().dtype(at::kByte));
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Tensor> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair((int)like.device().index(), st);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  Tensor t = at::zeros({nb}, like.options().dtype(at::kByte));
+  cache.emplace(key, t);
+  return t;
+}
+
 // ---------------- reference schemas ----------------
 Tensor int4_gemv(const Tensor& qweight, const Tensor& scales, const Tensor& x_in) {
   check_packed(qweight, scales, "int4_gemv");
@@ -84,7 +110,7 @@ Tensor topk_select(const Tensor& s_in, int64_t k) {
   TORCH_CHECK(k >= 0, "topk_select: k must be >= 0");
   Tensor idx = at::empty({k}, s.options().dtype(at::kInt));
   if (k == 0) return idx;
-  Tensor hist = at::zeros({(int64_t)dip_topk_hist_bytes()}, s.options().dtype(at::kByte));
+  Tensor hist = topk_hist_for(s);
   check_status(dip_topk_select_ws(bf(s), s.numel(), k, idx.data_ptr<int32_t>(), hist.data_ptr(),
                                   cur_stream()),
                "topk_select");
@@ -556,6 +582,67 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_ca(
                                k, ws_opt);
 }
 
+// one tensor-parallel layer on this rank (dip_mlp_decode_fused_tp); the
+// workspaces are raw device addresses (own + IPC-mapped peers)
+std::tuple<Tensor, Tensor> mlp_decode_fused_tp(
+    const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
+    const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
+    double eps, int64_t k, int64_t inter_total, int64_t rank, int64_t world,
+    at::IntArrayRef workspaces, int64_t workspace_bytes, const std::optional<Tensor>& idx_out,
+    const std::optional<Tensor>& x_used) {
+  check_packed(gate_qw, gate_sc, "mlp_decode_fused_tp(gate)");
+  check_packed(up_qw, up_sc, "mlp_decode_fused_tp(up)");
+  check_packed(dt_qw, dt_sc, "mlp_decode_fused_tp(down_t)");
+  c10::cuda::CUDAGuard guard(gate_qw.device());
+  Tensor x = x_in.contiguous();
+  check_dtype(x, at::kBFloat16, "x");
+  const int64_t hidden = gate_qw.size(1) * 2, inter = gate_qw.size(0);
+  TORCH_CHECK(x.numel() == hidden && up_qw.sizes() == gate_qw.sizes() &&
+                  dt_qw.size(0) == inter && dt_qw.size(1) * 2 == hidden,
+              "mlp_decode_fused_tp: shape mismatch");
+  TORCH_CHECK((int64_t)workspaces.size() == world, "mlp_decode_fused_tp: one workspace per rank");
+  Tensor r;
+  if (resid.has_value()) {
+    r = resid->contiguous();
+    check_dtype(r, at::kBFloat16, "resid");
+    TORCH_CHECK(r.numel() == hidden, "mlp_decode_fused_tp: resid size");
+  }
+  int32_t* idxp = nullptr;
+  if (idx_out.has_value()) {
+    TORCH_CHECK(idx_out->is_cuda() && idx_out->is_contiguous() &&
+                    idx_out->scalar_type() == at::kInt && idx_out->numel() == k,
+                "mlp_decode_fused_tp: idx_out must be a contiguous CUDA int32 [k] tensor");
+    idxp = idx_out->data_ptr<int32_t>();
+  }
+  dip_bf16* xu = nullptr;
+  if (x_used.has_value()) {
+    TORCH_CHECK(x_used->is_cuda() && x_used->is_contiguous() &&
+                    x_used->scalar_type() == at::kBFloat16 && x_used->numel() == hidden,
+                "mlp_decode_fused_tp: x_used must be a contiguous CUDA bf16 [hidden] tensor");
+    xu = reinterpret_cast<dip_bf16*>(x_used->data_ptr());
+  }
+  dip_layer_t L = {i8(gate_qw), bf(gate_sc), i8(up_qw), bf(up_sc), i8(dt_qw), bf(dt_sc),
+                   hidden, inter};
+  std::vector<void*> ws(workspaces.size());
+  for (size_t q = 0; q < ws.size(); ++q) ws[q] = reinterpret_cast<void*>(workspaces[q]);
+  Tensor y = bf16_empty(hidden, x), g = bf16_empty(inter, x);
+  check_status(dip_mlp_decode_fused_tp(&L, inter_total, (int)rank, (int)world, ws.data(),
+                                       (size_t)workspace_bytes, bf(x),
+                                       resid.has_value() ? bf(r) : nullptr, (float)eps, k, bfm(y),
+                                       bfm(g), idxp, xu, cur_stream()),
+               "mlp_decode_fused_tp");
+  return {y, g};
+}
+
+int64_t op_mlp_fused_tp_workspace_bytes(int64_t hidden, int64_t inter_total, int64_t k) {
+  return (int64_t)dip_mlp_fused_tp_workspace_bytes(hidden, inter_total, k);
+}
+
+int64_t op_set_spin_limit(int64_t polls) {
+  check_status(dip_set_spin_limit((unsigned)polls), "set_spin_limit");
+  return 0;
+}
+
 int64_t op_mlp_fused_workspace_bytes(int64_t hidden, int64_t inter, int64_t k) {
   return (int64_t)dip_mlp_fused_workspace_bytes(hidden, inter, k);
 }
@@ -619,6 +706,13 @@ TORCH_LIBRARY(dip_b200, m) {
       "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
   m.def("mlp_fused_workspace_bytes(int hidden, int inter, int k) -> int");
   m.def(
+      "mlp_decode_fused_tp(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
+      "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
+      "int inter_total, int rank, int world, int[] workspaces, int workspace_bytes, "
+      "Tensor? idx_out=None, Tensor? x_used=None) -> (Tensor, Tensor)");
+  m.def("mlp_fused_tp_workspace_bytes(int hidden, int inter_total, int k) -> int");
+  m.def("set_spin_limit(int polls) -> int");
+  m.def(
       "mlp_decode_fused_ca(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
       "Tensor down_t_qw, Tensor down_t_sc, Tensor id2slot, Tensor res_up_qw, Tensor res_up_sc, "
       "Tensor res_dn_qw, Tensor res_dn_sc, Tensor x, Tensor? resid, float eps, int k, "
@@ -653,6 +747,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("mlp_decode", &mlp_decode);
   m.impl("mlp_decode_fused", &mlp_decode_fused);
   m.impl("mlp_decode_fused_ca", &mlp_decode_fused_ca);
+  m.impl("mlp_decode_fused_tp", &mlp_decode_fused_tp);
   m.impl("quantize_int4", &quantize_int4);
   m.impl("dequantize_int4", &dequantize_int4);
   m.impl("transpose_down_int4", &transpose_down_int4);
@@ -669,6 +764,8 @@ TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) {
   m.impl("set_pdl", &op_set_pdl);
   m.impl("mlp_workspace_bytes", &op_mlp_workspace_bytes);
   m.impl("mlp_fused_workspace_bytes", &op_mlp_fused_workspace_bytes);
+  m.impl("mlp_fused_tp_workspace_bytes", &op_mlp_fused_tp_workspace_bytes);
+  m.impl("set_spin_limit", &op_set_spin_limit);
   m.impl("set_gemv_variant", &op_set_gemv_variant);
   m.impl("take_device_error", &op_take_device_error);
 }

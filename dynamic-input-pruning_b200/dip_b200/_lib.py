@@ -115,6 +115,12 @@ def _register_fakes_fused():
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))
 
+    @torch.library.register_fake("dip_b200::mlp_decode_fused_tp")
+    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, inter_total, rank, world, workspaces,
+          workspace_bytes, idx_out=None, x_used=None):
+        return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
+                torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device))
+
     @torch.library.register_fake("dip_b200::gemv_batched")
     def _(qweight, scales, x, silu):
         return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)

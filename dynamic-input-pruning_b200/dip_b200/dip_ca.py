@@ -2,15 +2,19 @@
 
 The reference keeps the most frequently selected channels' up/down rows
 resident on the GPU and streams the misses over PCIe (dip_ca.py:1-13).  On a
-B200 both the resident cache and the full weights sit in HBM; the per-token
-path is
+B200 both the resident cache and the full weights sit in HBM; a decode token
+is one persistent kernel (layer_fused_kernel with the cache: each selected
+channel's up and down rows come from its cache slot when id2slot has one,
+else from the full rows) where the shape allows it, else the separate
+launches
 
     gate GEMV + SiLU -> top-k -> hit/miss split (id2slot) ->
     dual-source up GEMV (h = g*u) -> dual-source down
 
 with the split computed on the device (no `.to("cpu")`, no host sync) in the
 reference's order: hits in idx order, then misses in idx order
-(dip_ca.py:137-142, 164-171).  Hits read the resident cache rows, misses the
+(dip_ca.py:137-142, 164-171); `last_split` gives that split for the last
+token either way.  Hits read the resident cache rows, misses the
 full resident rows.  Calibration and the deterministic hot-set key
 (count*I - id, dip_ca.py:306-308) are unchanged.
 """
@@ -25,6 +29,7 @@ from .qlinear import _require_cuda, dequantize
 from .gate_kernel import gate_gemv, gate_silu
 from .topk_kernel import select_topk
 from .dip_stream_predispatch import _transpose_down_to_int4
+from .fastpath import dense_mlp, fused_layer_supported
 
 load_ops()
 _use_ca_fused = True
@@ -72,8 +77,29 @@ class CADIPMlp(nn.Module):
         self._res_up_sc = None
         self._res_dn_qw = None
         self._res_dn_sc = None
+        self.last_g = None
         self.last_idx = None
-        self.last_split = None
+        self._last_split = None
+        self._fused = fused_layer_supported(self.out_features, self.inter, self.device)
+        self._ws = None  # fused decode workspace, zeroed once, left reusable
+
+    @property
+    def last_split(self):
+        """(combined_ids, src, row, n_hit) of the last decode token: hits then
+        misses, each in idx order (dip_ca.py:137-142, 164-171)."""
+        if self._last_split is None and self.last_idx is not None:
+            self._last_split = torch.ops.dip_b200.ca_split(self.last_idx, self.id2slot)
+        return self._last_split
+
+    @last_split.setter
+    def last_split(self, v):
+        self._last_split = v
+
+    def reset_workspace(self):
+        """Zero the decode workspace again (after the device error word
+        reported a bounded wait that ran out)."""
+        if self._ws is not None:
+            self._ws.zero_()
 
     def set_cache(self, hot_ids):
         """dip_ca.py:107-117: keep hot_ids[:cache_n] sorted ascending; id2slot[id]
@@ -97,8 +123,19 @@ class CADIPMlp(nn.Module):
         return F.linear(x, w)
 
     def decode_token(self, xf: torch.Tensor):
-        """One token: returns (y, g, idx, (combined_ids, src, row, n_hit))."""
+        """One token: returns (y, g, idx, (combined_ids, src, row, n_hit)); the
+        split is None on the one-launch path (computed on demand)."""
         xf = xf.reshape(-1).to(torch.bfloat16)
+        if self._fused:
+            if self._ws is None:
+                nb = torch.ops.dip_b200.mlp_fused_workspace_bytes(self.out_features, self.inter,
+                                                                  self.k)
+                self._ws = torch.zeros(nb, dtype=torch.uint8, device=self.device)
+            y, g, idx = torch.ops.dip_b200.mlp_decode_fused_ca(
+                self.gate_qw, self.gate_sc, self.up_qw, self.up_sc, self.down_t_qw,
+                self.down_t_sc, self.id2slot, self._res_up_qw, self._res_up_sc, self._res_dn_qw,
+                self._res_dn_sc, xf, None, 1e-6, self.k, self._ws)
+            return y, g, idx, None
         g = gate_silu(self.gate_qw, self.gate_sc, xf)
         idx = torch.ops.topk_ops.topk_select(g, self.k)
         comb, src, row, n_hit = torch.ops.dip_b200.ca_split(idx, self.id2slot)
@@ -117,11 +154,16 @@ class CADIPMlp(nn.Module):
         for b in range(x.shape[0]):
             y, g, idx, split = self.decode_token(x[b, 0])
             ys.append(y)
-        self.last_idx, self.last_split = idx, split
+        self.last_g, self.last_idx, self.last_split = g, idx, split
         return torch.stack(ys).to(x.dtype).reshape(x.shape[0], 1, -1)
 
     def _dense(self, x):
-        """dip_ca.py:190-196."""
+        """dip_ca.py:190-196, the GEMMs on the tensor cores where the shapes
+        allow (dequantize + F.linear otherwise)."""
+        y = dense_mlp(self.gate_qw, self.gate_sc, self.up_qw, self.up_sc, self.down_t_qw,
+                      self.down_t_sc, x)
+        if y is not None:
+            return y
         g = F.silu(self._gate(x))
         up_w = dequantize(self.up_qw, self.up_sc).to(x.dtype)
         u = F.linear(x, up_w)

@@ -2,13 +2,13 @@
 
 On the reference's T4 the up/down rows of the selected channels were gathered
 on the CPU and streamed over PCIe each token.  On a B200 the whole int4 model
-is resident in HBM, so StreamingDIPMlp keeps every weight on the GPU and the
-decode step is four kernels with no host synchronisation:
-
-    gate GEMV + SiLU -> top-k -> gathered up GEMV (h = g*u) -> gathered down
-
-(reference forward: dip_stream_predispatch.py:176-204).  Constructor
-signatures, attribute names and the _dense prefill path are kept.
+is resident in HBM, so StreamingDIPMlp keeps every weight on the GPU and a
+decode token is one persistent kernel (gate GEMV + SiLU, exact top-k,
+gathered up GEMV with h = g*u, gathered down; layer_fused_kernel) where the
+shape allows it, else four kernels with no host synchronisation (reference
+forward: dip_stream_predispatch.py:176-204).  Prefill (_dense) runs the
+dense GEMMs on the tcgen05 tensor cores.  Constructor signatures, attribute
+names and the _dense path are kept.
 """
 from __future__ import annotations
 
@@ -18,6 +18,7 @@ import torch.nn.functional as F
 
 from ._lib import load_ops
 from .qlinear import GROUP_SIZE, _require_cuda, dequantize
+from .fastpath import dense_mlp, fused_layer_supported
 from .gate_kernel import gate_gemv, _use_gate  # noqa: F401
 from .topk_kernel import select_topk, _use_topk  # noqa: F401
 
@@ -98,6 +99,8 @@ class StreamingDIPMlp(nn.Module):
         # Intermediates of the last decode call (device tensors, no sync).
         self.last_g = None
         self.last_idx = None
+        self._fused = fused_layer_supported(self.out_features, self.inter, self.device)
+        self._ws = None  # decode workspace, zeroed once, left reusable by every call
 
     def _gate(self, x):
         """dip_stream_predispatch.py:166-174."""
@@ -107,11 +110,29 @@ class StreamingDIPMlp(nn.Module):
         w = dequantize(self.gate_qw, self.gate_sc).to(x.dtype)
         return F.linear(x, w)
 
+    def _workspace(self):
+        if self._ws is None:
+            op = (torch.ops.dip_b200.mlp_fused_workspace_bytes if self._fused
+                  else torch.ops.dip_b200.mlp_workspace_bytes)
+            nb = op(self.out_features, self.inter, self.k)
+            self._ws = torch.zeros(nb, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def reset_workspace(self):
+        """Zero the decode workspace again (after the device error word
+        reported a bounded wait that ran out)."""
+        if self._ws is not None:
+            self._ws.zero_()
+
     def decode_token(self, xf: torch.Tensor):
         """One token [hidden] -> (y [hidden] bf16, g [inter] bf16, idx [k] int32)."""
-        return torch.ops.dip_b200.mlp_decode(self.gate_qw, self.gate_sc, self.up_qw,
-                                             self.up_sc, self.down_t_qw, self.down_t_sc,
-                                             xf.reshape(-1).to(torch.bfloat16), self.k)
+        xf = xf.reshape(-1).to(torch.bfloat16)
+        args = (self.gate_qw, self.gate_sc, self.up_qw, self.up_sc, self.down_t_qw,
+                self.down_t_sc)
+        if self._fused:
+            return torch.ops.dip_b200.mlp_decode_fused(*args, xf, None, 1e-6, self.k,
+                                                       self._workspace())
+        return torch.ops.dip_b200.mlp_decode(*args, xf, self.k, self._workspace())
 
     def forward(self, x):
         if x.dim() != 3 or x.shape[1] != 1 or self.keep_ratio >= 0.999:
@@ -128,7 +149,13 @@ class StreamingDIPMlp(nn.Module):
         return torch.stack(ys).to(xdt).reshape(x.shape[0], 1, -1)
 
     def _dense(self, x):
-        """dip_stream_predispatch.py:206-215 (prefill / keep_ratio ~ 1)."""
+        """dip_stream_predispatch.py:206-215 (prefill / keep_ratio ~ 1): the
+        three GEMMs on the tensor cores (dequantize + F.linear for shapes the
+        tcgen05 GEMMs do not take)."""
+        y = dense_mlp(self.gate_qw, self.gate_sc, self.up_qw, self.up_sc, self.down_t_qw,
+                      self.down_t_sc, x)
+        if y is not None:
+            return y
         g = F.silu(self._gate(x))
         up_w = dequantize(self.up_qw, self.up_sc).to(x.dtype)
         u = F.linear(x, up_w)

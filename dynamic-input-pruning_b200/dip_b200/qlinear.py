@@ -63,6 +63,10 @@ class QuantLinear(nn.Module):
             y = torch.ops.int4_ops.int4_gemv(self.qweight, self.scales,
                                              x.reshape(-1).to(torch.bfloat16))
             return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
+        from .fastpath import tc_linear, tc_linear_ok
+        if tc_linear_ok(self.in_features, x):  # tokens x rows GEMM on the tensor cores
+            y = tc_linear(self.qweight, self.scales, x.reshape(-1, self.in_features))
+            return y.reshape(*x.shape[:-1], self.out_features)
         w = dequantize(self.qweight, self.scales)
         return F.linear(x, w.to(x.dtype))
 

@@ -153,7 +153,7 @@ class DipStack:
             self._ws_fused = fused_ws
         if self.mode in ("ca", "ca_chain") and self.ca is None:
             raise RuntimeError("cache-aware mode needs calibrate_ca() first")
-        idxs, splits = [], []
+        idxs, splits, ys = [], [], []
         y = None
         for l, L in enumerate(self.layers):
             if self.mode == "fused":
@@ -192,10 +192,22 @@ class DipStack:
                         splits.append((comb, src, row, n_hit))
             if record:
                 idxs.append(idx)
+                ys.append(y)
         if record:
             self.last_idx = idxs
+            self.last_y = ys
             self.last_split = splits if self.mode in ("ca", "ca_chain") else None
         return y
+
+    def take_device_error(self) -> int:
+        """Reads and clears the library's device error word.  A nonzero value
+        means a bounded wait ran out: that call's outputs are invalid and the
+        workspace's selection state (histograms, counters) may be stale, so
+        the workspace is zeroed here before the next call."""
+        err = int(torch.ops.dip_b200.take_device_error())
+        if err and getattr(self, "_ws", None) is not None:
+            self._ws.zero_()
+        return err
 
     # -- one token, CUDA graph --------------------------------------------
     def capture(self) -> None:

@@ -24,6 +24,14 @@ P <= 8 at keep_ratio 0.6, a local pre-selection would prune nothing.
 The compute backend is pluggable so the orchestration (sharding, collectives,
 merge) can be exercised by CPU tests with a `gloo` group; the default backend
 is the sm_100a kernels.
+
+`TPFusedStack` is the fast form of the same sharded layer: ONE cooperative
+kernel per layer and rank (dip_mlp_decode_fused_tp) in which the exchange is
+part of the kernel.  Each rank's gate CTAs add their |g| keys to every rank's
+selection histograms over NVLink, so every rank finds the same selection
+without moving g; after the gathered down projection each CTA stores its
+quads of the fp32 partial y into every rank's y slots and sums the slots in
+rank order.  No all-gather of g and no separate all-reduce launch.
 """
 from __future__ import annotations
 
@@ -230,3 +238,155 @@ class TPDipStack:
     def replay(self):
         self._graph.replay()
         return self._static_out
+
+
+def _sm_count(device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
+class TPFusedWorkspace:
+    """The per-rank workspace of the tensor-parallel fused layer: allocated
+    zeroed by the library (dip_p2p_alloc), its CUDA IPC handle shared through
+    the process group and the peers' workspaces mapped over NVLink
+    (dip_ipc_open).  `ptrs[q]` is rank q's workspace as this process maps it.
+    One workspace serves every layer (the layers run one after another)."""
+
+    def __init__(self, hidden: int, inter_total: int, k: int, device, group=None):
+        import ctypes
+        from ._lib import core
+        self.lib = lib = core()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.device = torch.device(device)
+        vp = ctypes.c_void_p
+        lib.dip_p2p_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        lib.dip_ipc_handle.argtypes = [vp, ctypes.c_char_p]
+        lib.dip_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
+        lib.dip_ipc_close.argtypes = [vp]
+        lib.dip_p2p_free.argtypes = [vp]
+        self.nbytes = int(torch.ops.dip_b200.mlp_fused_tp_workspace_bytes(hidden, inter_total, k))
+        with torch.cuda.device(self.device):
+            mine = vp()
+            P2PExchange._check(lib.dip_p2p_alloc(self.nbytes, ctypes.byref(mine)), "dip_p2p_alloc")
+            handle = ctypes.create_string_buffer(64)
+            P2PExchange._check(lib.dip_ipc_handle(mine, handle), "dip_ipc_handle")
+            info = [None] * self.world
+            dist.all_gather_object(info, (handle.raw, _sm_count(self.device), self.nbytes),
+                                   group=group)
+            if len({(n, b) for _, n, b in info}) != 1:
+                raise RuntimeError(f"tensor-parallel ranks disagree on SM count / workspace size: "
+                                   f"{[(n, b) for _, n, b in info]}")
+            ptrs, self._opened = [], []
+            for q, (hq, _, _) in enumerate(info):
+                if q == self.rank:
+                    ptrs.append(mine.value)
+                    continue
+                pq = vp()
+                P2PExchange._check(lib.dip_ipc_open(ctypes.create_string_buffer(hq, 64),
+                                                    ctypes.byref(pq)), "dip_ipc_open")
+                ptrs.append(pq.value)
+                self._opened.append(pq.value)
+        self.ptrs = ptrs
+        self._mine = mine.value
+        self.view = torch.as_tensor(_DeviceView(mine.value, self.nbytes, "|u1"), device=self.device)
+        dist.barrier(group=group)
+
+    def zero_(self) -> None:
+        """Clears this rank's workspace (needed after a device-side timeout;
+        every rank must clear its own before the next call)."""
+        self.view.zero_()
+
+
+class TPFusedStack:
+    """Config 4 on the one-launch TP layer: the synthetic 64-layer stack with
+    every layer sharded along I over the process group (rank r keeps rows
+    [r I/P, (r+1) I/P) of gate, up and down_t), one dip_mlp_decode_fused_tp
+    launch per layer and rank.  The inter-layer step RMSNorm(y + r) is folded
+    into the next layer's kernel, as in DipStack's fused mode; y is identical
+    on every rank.  keep_full keeps each layer's unsharded weights too (the
+    in-run check against one GPU)."""
+
+    def __init__(self, cfg, device, group=None, keep_full: bool = False):
+        from .stack import make_layer
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if cfg.inter % self.world:
+            raise ValueError(f"intermediate size {cfg.inter} is not divisible by {self.world} ranks")
+        self.ws = TPFusedWorkspace(cfg.hidden, cfg.inter, cfg.k, self.device, group)
+        self.shards, self.full = [], [] if keep_full else None
+        for l in range(cfg.n_layers):
+            full = make_layer(cfg, l, self.device)
+            self.shards.append(shard_layer(full, self.rank, self.world))
+            if keep_full:
+                self.full.append(full)
+            del full
+        torch.cuda.empty_cache()
+        self._graph = None
+        self._static_in = None
+        self._static_out = None
+        self.last_idx = None
+        self.last_x = None
+
+    def step(self, x0, resid, record=False):
+        """x0 [H], resid [L, H] -> last y [H].  With record, also the per-layer
+        inputs (as the kernels normalised them) and the full index lists
+        (every rank's entries, summed over the group)."""
+        from .stack import RMS_EPS
+        cfg, ws = self.cfg, self.ws
+        y = None
+        idxs, xs = [], []
+        for l, s in enumerate(self.shards):
+            xin, r = (x0, None) if l == 0 else (y, resid[l])
+            idx = xu = None
+            if record:
+                idx = torch.zeros(cfg.k, dtype=torch.int32, device=self.device)
+                xu = torch.empty(cfg.hidden, dtype=torch.bfloat16, device=self.device)
+            y, _ = torch.ops.dip_b200.mlp_decode_fused_tp(
+                s["gate_qw"], s["gate_sc"], s["up_qw"], s["up_sc"], s["down_t_qw"],
+                s["down_t_sc"], xin, r, RMS_EPS, cfg.k, cfg.inter, self.rank, self.world,
+                ws.ptrs, ws.nbytes, idx, xu)
+            if record:
+                idxs.append(idx)
+                xs.append(xu)
+        if record:
+            allidx = torch.stack(idxs)
+            dist.all_reduce(allidx, op=dist.ReduceOp.SUM, group=self.group)
+            self.last_idx = list(allidx)
+            self.last_x = xs
+        return y
+
+    def capture(self):
+        H, n = self.cfg.hidden, self.cfg.n_layers
+        self._static_in = (torch.zeros(H, dtype=torch.bfloat16, device=self.device),
+                           torch.zeros(n, H, dtype=torch.bfloat16, device=self.device))
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.step(*self._static_in)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._static_out = self.step(*self._static_in)
+        self._graph = g
+
+    def replay(self):
+        self._graph.replay()
+        return self._static_out
+
+    def decode(self, x0: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+        """Public call (every rank): one token through every layer; host
+        inputs are copied in, the result comes back to the host."""
+        if self._graph is None:
+            self.capture()
+        xi, ri = self._static_in
+        xi.copy_(x0, non_blocking=True)
+        ri.copy_(resid, non_blocking=True)
+        out = self.replay()
+        if x0.device.type == "cpu":
+            res = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            res.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            return res
+        return out

@@ -56,6 +56,15 @@ DIP_API int dip_set_pdl(int enable);
  * completed) and returned early; its outputs are then invalid.  Synchronous
  * (a device-to-host copy).  0 = no error recorded. */
 DIP_API int dip_take_device_error(unsigned int* out);
+/* Sets the poll limit of every bounded device wait (grid barriers, the fused
+ * layer's selection hand-offs, the peer-memory exchanges) on the current
+ * device; 0 restores the compiled default (2^24 polls).  A wait that runs out
+ * sets bit 0 of the device error word and the kernel returns; its outputs and
+ * the workspace's selection state are then invalid (zero the workspace
+ * before reusing it).  No counterpart in the reference (it has no device
+ * waits); exists so that callers and tests can bound how long a missing peer
+ * can hold a kernel.  Synchronous. */
+DIP_API int dip_set_spin_limit(unsigned int polls);
 /* Selects the kernel implementations: 0 (default) = the streaming kernels
  * (K-slice cp.async GEMV family and tensor-core down projection) where the
  * shape allows them, 1 = the simple kernels (one tile per CTA GEMV, CUDA-core
@@ -320,6 +329,40 @@ DIP_API int dip_p2p_gather(int rank, int world, void* const* mailboxes, const di
                            int64_t n_local, int64_t hidden, dip_stream_t stream);
 DIP_API int dip_p2p_reduce(int rank, int world, void* const* mailboxes, const float* partial,
                            int64_t inter, int64_t hidden, dip_bf16* y, dip_stream_t stream);
+/* Mailboxes handed to dip_p2p_gather / dip_p2p_reduce / dip_mlp_decode_fused_tp
+ * for peers must come from dip_p2p_alloc (own) or dip_ipc_open (peers): the
+ * library records each range's size and rejects (DIP_ERR_ARG) a call whose
+ * stores would not fit, instead of writing past another GPU's allocation. */
+
+/* ---- a5..a10 sharded along I, one launch per rank: the tensor-parallel layer ----
+ * StreamingDIPMlp.forward (dip_stream_predispatch.py:176-204) for one token with
+ * the channels split over `world` GPUs: rank r holds rows [r I/P, (r+1) I/P) of
+ * gate, up and the transposed down (`shard`, shard->inter = I/P) and runs one
+ * cooperative kernel per layer that
+ *   - computes its g slice and adds its |g| keys to every rank's histograms
+ *     (remote reductions over NVLink), so every rank's coordinating CTA finds
+ *     the same selection over all inter_total channels (indices identical to
+ *     dip_mlp_decode_fused's on the whole layer);
+ *   - gathers up / down over its own selected channels;
+ *   - stores its fp32 partial of y into every rank's y slots (16-byte peer
+ *     stores plus a tagged flag per CTA) and sums the slots in rank order:
+ *     y is identical on every rank.
+ * No NCCL, no multicast, no TMA on peer memory: peer stores, peer reductions
+ * and local polls only.  workspaces[q] = rank q's workspace
+ * (dip_mlp_fused_tp_workspace_bytes, zeroed before the first call, 256-byte
+ * aligned; peers' mapped through dip_ipc_open).  Every rank makes the same
+ * sequence of calls with the same shapes on GPUs with the same SM count.
+ * idx_out (optional, [k]) receives only the entries of this rank's channels
+ * (global channel ids at their global positions; rank 0 also writes the zero
+ * padding); g_out (optional) this rank's g slice.  Waits are bounded (device
+ * error word; after a timeout zero every rank's workspace).  No counterpart in
+ * the reference, which is single-GPU. */
+DIP_API size_t dip_mlp_fused_tp_workspace_bytes(int64_t hidden, int64_t inter_total, int64_t k);
+DIP_API int dip_mlp_decode_fused_tp(const dip_layer_t* shard, int64_t inter_total, int rank,
+                                    int world, void* const* workspaces, size_t workspace_bytes,
+                                    const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
+                                    dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
+                                    dip_bf16* x_used, dip_stream_t stream);
 
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit

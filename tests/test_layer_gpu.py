@@ -187,10 +187,15 @@ def test_ca_dip_module(dip, oracle, small_layer, dev):
     assert torch.equal(comb.cpu(), rc) and torch.equal(src.cpu(), rs)
     assert torch.equal(row.cpu(), rr) and n_hit.item() == rn
     assert 0 < rn < m.k
-    r = oracle.ca_mlp_decode(x.reshape(-1), L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"],
-                             L["down_t_qw"], L["down_t_sc"], m.k, id2slot)
-    if torch.equal(r["idx"], m.last_idx.cpu()):
-        close(y.reshape(-1), r["y_f32"])
+    # g within tolerance, idx exact given the module's g, y against the
+    # oracle chain run from the module's own g over the combined order
+    g = m.last_g.cpu()
+    close(g, oracle.silu_bf16(oracle.int4_gemv(L["gate_qw"], L["gate_sc"], x.reshape(-1))))
+    assert torch.equal(m.last_idx.cpu(), oracle.topk_select(g, m.k))
+    cl = comb.cpu().long()
+    u = oracle.int4_gemv(L["up_qw"], L["up_sc"], x.reshape(-1), rows=cl)
+    h = (g[cl].float() * u.float()).to(torch.bfloat16)
+    close(y.reshape(-1), oracle.gather_down_f32(L["down_t_qw"], L["down_t_sc"], h, rows=cl))
     # CA output equals the streaming module's up to summation order
     shared = dip.SharedBuffers(m.k, 512, 8, 1024, 8, dev)
     s = dip.StreamingDIPMlp(L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_qw"],
@@ -210,3 +215,64 @@ def test_quantlinear(dip, oracle, dev):
     xs = torch.randn(4, 512, generator=gen).to(torch.bfloat16)
     ref = xs.float() @ oracle.dequantize(qw, sc).float().t()
     close(ql(xs.to(dev)), ref)
+
+
+# ------------------------------------------- drop-in modules on the fast paths
+@pytest.fixture(scope="module")
+def fused_shape_layer(oracle):
+    """hidden 2560, inter 8192: a shape the one-launch fused layer takes."""
+    return oracle.make_layer_cpu(2560, 8192, seed=21)
+
+
+def test_modules_decode_on_fused_layer(dip, oracle, fused_shape_layer, dev):
+    L = fused_shape_layer
+    k = int(round(8192 * 0.6))
+    shared = dip.SharedBuffers(k, 1280, 20, 2560, 20, dev)
+    m = dip.StreamingDIPMlp(L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_qw"],
+                            L["down_sc"], shared, 0.6, dev)
+    assert m._fused
+    gen = torch.Generator().manual_seed(3)
+    for t in range(2):  # the module-owned workspace is reused
+        x = torch.randn(1, 1, 2560, generator=gen).to(torch.bfloat16)
+        y = m(x.to(dev))
+        g = m.last_g.cpu()
+        close(g, oracle.silu_bf16(oracle.int4_gemv(L["gate_qw"], L["gate_sc"], x.reshape(-1))))
+        assert torch.equal(m.last_idx.cpu(), oracle.topk_select(g, k))
+        il = m.last_idx.cpu().long()
+        u = oracle.int4_gemv(L["up_qw"], L["up_sc"], x.reshape(-1), rows=il)
+        h = (g[il].float() * u.float()).to(torch.bfloat16)
+        close(y.reshape(-1), oracle.gather_down_f32(L["down_t_qw"], L["down_t_sc"], h, rows=il))
+    # cache-aware module on the same weights: same g / idx, split exact
+    buf = dip.CABuffers(k, 1280, 20, 2560, 20, dev)
+    c = dip.CADIPMlp(L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_qw"],
+                     L["down_sc"], buf, 0.6, 0.3, dev)
+    calib = torch.randn(1, 16, 2560, generator=gen).to(torch.bfloat16)
+    dip.calibrate_cache_inputs([c], calib.to(dev))
+    assert c._fused
+    yc = c(x.to(dev))
+    assert torch.equal(c.last_idx, m.last_idx) and torch.equal(c.last_g, m.last_g)
+    comb, src, row, n_hit = c.last_split
+    rc, rs, rr, rn = oracle.ca_split(c.last_idx.cpu(), c.id2slot.cpu())
+    assert torch.equal(comb.cpu(), rc) and torch.equal(src.cpu(), rs)
+    assert torch.equal(row.cpu(), rr) and int(n_hit) == rn and 0 < rn < k
+    close(yc, y)
+
+
+def test_dense_prefill_on_tensor_cores(dip, oracle, fused_shape_layer, dev):
+    """_dense (dip_stream_predispatch.py:206-215) for a 5-token prefill: the
+    tcgen05 GEMMs against the reference's dequantize + F.linear math in fp32."""
+    L = fused_shape_layer
+    k = int(round(8192 * 0.6))
+    shared = dip.SharedBuffers(k, 1280, 20, 2560, 20, dev)
+    m = dip.StreamingDIPMlp(L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_qw"],
+                            L["down_sc"], shared, 0.6, dev)
+    x = torch.randn(1, 5, 2560, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    y = m(x.to(dev))
+    assert y.shape == (1, 5, 2560)
+    xf = x.reshape(5, 2560).float()
+    g = torch.nn.functional.silu(
+        (xf @ oracle.dequantize(L["gate_qw"], L["gate_sc"]).float().t()).to(torch.bfloat16))
+    u = (xf @ oracle.dequantize(L["up_qw"], L["up_sc"]).float().t()).to(torch.bfloat16)
+    h = (g * u).to(torch.bfloat16)
+    ref = h.float() @ oracle.dequantize(L["down_t_qw"], L["down_t_sc"]).float()
+    close(y.reshape(5, 2560), ref)
