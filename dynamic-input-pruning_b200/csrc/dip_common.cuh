@@ -182,7 +182,7 @@ int gather_down_clear(const int8_t* down_t, const uint16_t* scales, int64_t n_ro
 
 namespace dip {
 // ---------------------------------------------------------------------------
-// mbarrier + bulk-copy (TMA, non-tensor, no multicast) helpers.  Every wait
+// mbarrier + bulk-copy (TMA, non-tensor, copies into this CTA only) helpers.  Every wait
 // is bounded: after kSpinLimit polls it ORs an error code into the device
 // error word (a kernel argument, see error_word_ptr) and reports failure
 // instead of hanging.

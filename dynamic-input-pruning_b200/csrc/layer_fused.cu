@@ -64,6 +64,7 @@ struct LfArgs {
   float* partial;           // [gridDim.x][hidden]
   uint16_t* y;              // [hidden]
   float* y_f32;             // optional
+  uint16_t* h_out;          // optional [inter_total]: h of each selected channel, by channel id
   GridBar* bar;
   unsigned* err;
   // cache-aware DIP (dip_ca.py:127-188), optional: channel c's up and down
@@ -837,6 +838,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         float v = 0.f;
         for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
         h = round_bf16(dh[r] * round_bf16(v));
+        if (a.h_out) a.h_out[(TP ? a.c0 : 0) + drow[r]] = f32_to_bf16_bits(h);
         if (r == pad_row) h *= mult;
       }
       dh[r] = h;
@@ -1410,6 +1412,15 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
                                        int64_t k, void* workspace, size_t workspace_bytes,
                                        dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
                                        dip_bf16* x_used, dip_stream_t stream) {
+  return dip_mlp_decode_fused_ex(L, cache, x, resid, eps, k, workspace, workspace_bytes, y, g_out,
+                                 idx_out, x_used, nullptr, stream);
+}
+
+extern "C" int dip_mlp_decode_fused_ex(const dip_layer_t* L, const dip_ca_cache_t* cache,
+                                       const dip_bf16* x, const dip_bf16* resid, float eps,
+                                       int64_t k, void* workspace, size_t workspace_bytes,
+                                       dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
+                                       dip_bf16* x_used, dip_bf16* h_out, dip_stream_t stream) {
   if (!L || !x || !y || !workspace) return DIP_ERR_ARG;
   if (cache && (!cache->id2slot || !cache->res_up_qw || !cache->res_up_sc || !cache->res_dn_qw ||
                 !cache->res_dn_sc))
@@ -1432,6 +1443,7 @@ extern "C" int dip_mlp_decode_fused_ca(const dip_layer_t* L, const dip_ca_cache_
   LfArgs a = {};
   lf_fill_common(a, L, static_cast<uint8_t*>(workspace), lay, x, resid, eps, k, y, g_out, idx_out,
                  x_used);
+  a.h_out = h_out;
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
   if (cache) {

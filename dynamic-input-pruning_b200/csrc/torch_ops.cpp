@@ -521,7 +521,8 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
 std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
     const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
     const Tensor& dt_qw, const Tensor& dt_sc, const dip_ca_cache_t* cache, const Tensor& x_in,
-    const std::optional<Tensor>& resid, double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
+    const std::optional<Tensor>& resid, double eps, int64_t k, const std::optional<Tensor>& ws_opt,
+    const std::optional<Tensor>& h_out = std::nullopt) {
   check_packed(gate_qw, gate_sc, "mlp_decode_fused(gate)");
   check_packed(up_qw, up_sc, "mlp_decode_fused(up)");
   check_packed(dt_qw, dt_sc, "mlp_decode_fused(down_t)");
@@ -546,9 +547,16 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
   Tensor ws = ws_opt.has_value() ? *ws_opt : at::zeros({(int64_t)wsb}, x.options().dtype(at::kByte));
   TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && (size_t)ws.nbytes() >= wsb,
               "mlp_decode_fused: workspace too small (need ", wsb, " bytes)");
-  check_status(dip_mlp_decode_fused_ca(&L, cache, bf(x), resid.has_value() ? bf(r) : nullptr,
+  dip_bf16* hp = nullptr;
+  if (h_out.has_value()) {
+    TORCH_CHECK(h_out->is_cuda() && h_out->is_contiguous() &&
+                    h_out->scalar_type() == at::kBFloat16 && h_out->numel() == inter,
+                "mlp_decode_fused: h_out must be a contiguous CUDA bf16 [inter] tensor");
+    hp = reinterpret_cast<dip_bf16*>(h_out->data_ptr());
+  }
+  check_status(dip_mlp_decode_fused_ex(&L, cache, bf(x), resid.has_value() ? bf(r) : nullptr,
                                        (float)eps, k, ws.data_ptr(), wsb, bfm(y), bfm(g),
-                                       idx.data_ptr<int32_t>(), nullptr, cur_stream()),
+                                       idx.data_ptr<int32_t>(), nullptr, hp, cur_stream()),
                "mlp_decode_fused");
   return {y, g, idx};
 }
@@ -556,9 +564,9 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
 std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
     const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
     const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
-    double eps, int64_t k, const std::optional<Tensor>& ws_opt) {
+    double eps, int64_t k, const std::optional<Tensor>& ws_opt, const std::optional<Tensor>& h_out) {
   return mlp_decode_fused_impl(gate_qw, gate_sc, up_qw, up_sc, dt_qw, dt_sc, nullptr, x_in, resid,
-                               eps, k, ws_opt);
+                               eps, k, ws_opt, h_out);
 }
 
 // the cache-aware layer in one launch (dip_mlp_decode_fused_ca)
@@ -703,7 +711,7 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def(
       "mlp_decode_fused(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
       "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
-      "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
+      "Tensor? workspace=None, Tensor? h_out=None) -> (Tensor, Tensor, Tensor)");
   m.def("mlp_fused_workspace_bytes(int hidden, int inter, int k) -> int");
   m.def(
       "mlp_decode_fused_tp(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "

@@ -103,7 +103,7 @@ def _register_fakes() -> None:
 
 def _register_fakes_fused():
     @torch.library.register_fake("dip_b200::mlp_decode_fused")
-    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, workspace=None):
+    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, workspace=None, h_out=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))

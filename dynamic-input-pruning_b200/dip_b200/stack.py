@@ -103,6 +103,18 @@ class DipStack:
         self.last_split = None
         self.ca = None  # per layer: id2slot, cache_ids and resident rows
 
+    @classmethod
+    def from_checkpoint(cls, ckpt_dir, device="cuda:0", n_layers: int | None = None,
+                        keep_ratio: float = 0.6, mode: str = "fused") -> "DipStack":
+        """A stack on the MLP weights of an int4 checkpoint written by the
+        reference's scripts/quantize.py (model_int4.safetensors +
+        quant_config.json), layers 0 .. n_layers-1."""
+        from .checkpoint import load_mlp_layers
+        layers = load_mlp_layers(ckpt_dir, device, n_layers)
+        I, H = layers[0]["gate_qw"].shape[0], layers[0]["gate_qw"].shape[1] * 2
+        cfg = StackConfig(n_layers=len(layers), hidden=H, inter=I, keep_ratio=keep_ratio)
+        return cls(cfg, device, layers=layers, mode=mode)
+
     # -- cache-aware DIP ---------------------------------------------------
     def calibrate_ca(self, x0s: torch.Tensor, resids: torch.Tensor) -> list:
         """Runs the tokens x0s [T, H] (residuals [T, L, H]) through the DIP

@@ -264,6 +264,16 @@ DIP_API int dip_mlp_decode_fused_ca(const dip_layer_t* layer, const dip_ca_cache
                                     void* workspace, size_t workspace_bytes, dip_bf16* y,
                                     dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
                                     dip_stream_t stream);
+/* As dip_mlp_decode_fused_ca, plus h_out (optional, [inter] bf16): for every
+ * selected channel c, h_out[c] = bf16(g[c] * bf16(u[c])), the h_sel of
+ * dip_stream_predispatch.py:201 that the down projection consumes (entries
+ * of unselected channels are left untouched).  Lets a caller check the up
+ * stage and the down stage of the one-launch layer separately. */
+DIP_API int dip_mlp_decode_fused_ex(const dip_layer_t* layer, const dip_ca_cache_t* cache,
+                                    const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
+                                    void* workspace, size_t workspace_bytes, dip_bf16* y,
+                                    dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
+                                    dip_bf16* h_out, dip_stream_t stream);
 
 /* ---- batched decode and dense forward on tcgen05 tensor cores ------------------
  * The reference decode path is batch-1 (dip_stream_predispatch.py:170, :182); a
