@@ -47,6 +47,7 @@ constexpr int kLfTilesA = 12;   // max gate tiles (16 rows) per CTA
 constexpr int kLfDnPitch = 144;  // bytes per channel row of a down slot (128 + pad)
 constexpr int kLfMaxCtas = 160;  // CTAs per grid (SMs per GPU) supported
 constexpr int kLfMaxRanks = 8;   // tensor-parallel ranks supported
+constexpr int kLfPfTiles = 3;    // next-layer gate tiles per worker moved into L2
 
 struct LfSel;
 struct LfArgs {
@@ -65,6 +66,9 @@ struct LfArgs {
   uint16_t* y;              // [hidden]
   float* y_f32;             // optional
   uint16_t* h_out;          // optional [inter_total]: h of each selected channel, by channel id
+  // optional: the next layer's gate weights (same shape); each worker moves
+  // the first rows of its range into L2 once its own work is done
+  const uint8_t* pf_qw; const uint16_t* pf_sc;
   GridBar* bar;
   unsigned* err;
   // cache-aware DIP (dip_ca.py:127-188), optional: channel c's up and down
@@ -150,6 +154,19 @@ __device__ __forceinline__ void cp_async4_lf(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem)
                : "memory");
 }
+// As cp_async16_lf / cp_async4_lf, but an invalid source writes zeros and
+// reads nothing (src-size 0): the padding rows of a partial tile cost no
+// memory request.  The address must still be a valid one (a real row).
+__device__ __forceinline__ void cp_async16_zf(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4_zf(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
 __device__ __forceinline__ void cp_commit_lf() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_lf() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(kLfDepth - 1) : "memory");
@@ -199,26 +216,28 @@ __device__ __forceinline__ void lf_tile_dot(const uint8_t* slot, const uint32_t 
 // x 16 bytes.  With GW == 2 a warp's slice of a row is one aligned 128-byte
 // line, so each instruction fetches 4 whole lines (8 lanes per row); with
 // GW == 1 it is 64 bytes (4 lanes per row, 8 rows per instruction).
+// Rows r >= nvalid are tile padding: zero-filled, not read.
 template <int GW, class QRow, class SRow>
-__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, QRow qrow, SRow srow, int warp, int lane) {
+__device__ __forceinline__ void lf_issue_gemv(uint8_t* slot, QRow qrow, SRow srow, int nvalid,
+                                              int warp, int lane) {
   if (GW == 2) {
     const int rsub = lane >> 3, c = lane & 7, gi = c >> 2, tq = c & 3;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int r = 4 * j + rsub;
-      cp_async16_lf(slot + (gi * 2 + (r >> 3)) * 512 + ((r & 7) * 4 + tq) * 16,
-                    qrow(r) + warp * 128 + c * 16);
+      cp_async16_zf(slot + (gi * 2 + (r >> 3)) * 512 + ((r & 7) * 4 + tq) * 16,
+                    qrow(r) + warp * 128 + c * 16, r < nvalid);
     }
   } else {
     const int gq = lane >> 2, tq = lane & 3;
     const int off = warp * kGroupBytes + tq * 16;
-    cp_async16_lf(slot + lane * 16, qrow(gq) + off);
-    cp_async16_lf(slot + 512 + lane * 16, qrow(gq + 8) + off);
+    cp_async16_zf(slot + lane * 16, qrow(gq) + off, gq < nvalid);
+    cp_async16_zf(slot + 512 + lane * 16, qrow(gq + 8) + off, gq + 8 < nvalid);
   }
   if (lane < 16) {
     // GW == 2: the 4 bytes [4 warp, 4 warp + 4); GW == 1: 2 bytes, copy the
     // aligned 4-byte word containing them.
-    cp_async4_lf(slot + GW * 1024 + lane * 4, srow(lane) + ((warp * GW) & ~1));
+    cp_async4_zf(slot + GW * 1024 + lane * 4, srow(lane) + ((warp * GW) & ~1), lane < nvalid);
   }
 }
 
@@ -606,7 +625,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot,
                         [&](int r) { return a.gate_qw + (size_t)min(rbase + r, rlast) * rowb; },
                         [&](int r) { return a.gate_sc + (size_t)min(rbase + r, rlast) * scw; },
-                        warp, lane);
+                        ra1 - rbase, warp, lane);
     }
     cp_commit_lf();
   };
@@ -824,6 +843,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   __shared__ int s_par[4];
   __shared__ int s_n[2];
   int nC = nts, nD = 0, nDA = 0;
+  int nCvalid = nts * 16;  // real rows of the C list (the rest is tile padding)
   bool have1 = false, have2 = false, c_done = false;
   // h = bf16(g * bf16(u)) for down list entries [r0, r1) once their up sums
   // are complete (entries hold g until then)
@@ -861,7 +881,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   auto issue_c = [&](int i) {
     const int* rp = crow + i * 16;
     lf_issue_gemv<GW>(ring + (i % kLfDepth) * Geo::slot, [&](int r) { return up_q(rp[r]); },
-                      [&](int r) { return up_s(rp[r]); }, warp, lane);
+                      [&](int r) { return up_s(rp[r]); }, nCvalid - i * 16, warp, lane);
   };
   const int seg = warp * GW * kGroupBytes;
   auto issue_d = [&](int j) {  // j: stream index; D tile j - nC
@@ -874,13 +894,15 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       const int ch = drow[i * 16 + r];
       const int sl = slot_of(ch);
       const uint8_t* row = sl >= 0 ? a.res_dn_qw + (size_t)sl * rowb : a.dn_qw + (size_t)ch * rowb;
-      cp_async16_lf(slot + r * kLfDnPitch + part * 16, row + seg + part * 16);
+      // padding entries (dsrc < 0) carry h = 0: zero-fill, no read
+      cp_async16_zf(slot + r * kLfDnPitch + part * 16, row + seg + part * 16, dsrc[i * 16 + r] >= 0);
     }
     if (lane < 16) {
       const int ch = drow[i * 16 + lane];
       const int sl = slot_of(ch);
       const uint16_t* srow = sl >= 0 ? a.res_dn_sc + (size_t)sl * scw : a.dn_sc + (size_t)ch * scw;
-      cp_async4_lf(slot + 16 * kLfDnPitch + lane * 4, srow + ((warp * GW) & ~1));
+      cp_async4_zf(slot + 16 * kLfDnPitch + lane * 4, srow + ((warp * GW) & ~1),
+                   dsrc[i * 16 + lane] >= 0);
     }
   };
   auto issue = [&](int j) {
@@ -965,6 +987,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       dh[offAB.x] = bf16_bits_to_f32(gloc[tid]);
     }
     nC = nts + ntr;
+    nCvalid = nts * 16 + nrest;
     nDA = totAB.x;
     nD = nDA / 16;  // the full tier A tiles need no release 2
     if (tid == 0) s_n[0] = -1;
@@ -1038,6 +1061,12 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   };
   // Per stream index j: wait for tile j, issue tile j + kLfDepth - 1 (into
   // the slot tile j - 1 used), compute tile j.
+  // The first speculative up tiles are requested before the histogram
+  // atomics below: requests queued behind ~500 same-address atomics per SM
+  // landed ~6 us after the gate instead of ~2 us.
+  const int npre = min(nts, kLfDepth - 1);
+#pragma unroll 1
+  for (int j = 0; j < npre; ++j) issue(j);  // j < nts: no release needed
   // This CTA's part of the global histograms: one relaxed atomic per distinct
   // key and coarse bin, no fence and no arrival flag (the coordinator checks
   // the totals), then the stream goes on at once.
@@ -1068,7 +1097,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
   }
 #pragma unroll 1
-  for (int j = 0; j < kLfDepth - 1; ++j) { need(j); issue(j); }
+  for (int j = npre; j < kLfDepth - 1; ++j) { need(j); issue(j); }
   for (int j = 0; j < nC; ++j) {
     cp_wait_lf2();
     __syncwarp();
@@ -1164,6 +1193,27 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       for (int q = 0; q < 4; ++q)
         reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
+  }
+  // The next layer's first gate tiles of this worker's rows go to L2 now:
+  // DRAM is mostly idle while the slowest workers finish and during the
+  // final barrier and reduction, and the next launch's first tiles then
+  // come from L2 (one bulk prefetch per range, issued by one thread).
+  // A bulk prefetch needs a 16-byte aligned start and a multiple of 16
+  // bytes: packed rows are (hidden / 2 is a multiple of 64), but a scale
+  // row is hidden / 64 bytes (40 at hidden 2560), so the scale range is
+  // widened to 16-byte boundaries and clamped to the scale tensor, whose
+  // size (inter * hidden / 64, inter a multiple of 8) is a multiple of 16.
+  if (a.pf_qw && tid == 0) {
+    const int nr = min(na, 16 * kLfPfTiles);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.pf_qw + (size_t)ra0 * rowb),
+                 "r"(nr * rowb) : "memory");
+    const size_t s_end = (size_t)I * scw * 2;
+    const size_t s0 = ((size_t)ra0 * scw * 2) & ~size_t(15);
+    const size_t s1 = min(s_end, ((size_t)(ra0 + nr) * scw * 2 + 15) & ~size_t(15));
+    if (s1 > s0)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n"
+                   ::"l"(reinterpret_cast<const uint8_t*>(a.pf_sc) + s0), "r"((unsigned)(s1 - s0))
+                   : "memory");
   }
   }  // worker
   pdl_launch_dependents();
@@ -1313,6 +1363,19 @@ static int lf_check_shape(int64_t H, int64_t I, int64_t IT, int64_t k, int nb, i
   return DIP_OK;
 }
 
+// Optional extras of a call; false if they are malformed.
+static bool lf_apply_opts(LfArgs& a, const dip_fused_opts_t* o) {
+  if (!o) return true;
+  a.h_out = o->h_out;
+  if ((o->prefetch_gate_qw == nullptr) != (o->prefetch_gate_sc == nullptr)) return false;
+  if ((reinterpret_cast<uintptr_t>(o->prefetch_gate_qw) |
+       reinterpret_cast<uintptr_t>(o->prefetch_gate_sc)) & 15)
+    return false;
+  a.pf_qw = reinterpret_cast<const uint8_t*>(o->prefetch_gate_qw);
+  a.pf_sc = o->prefetch_gate_sc;
+  return true;
+}
+
 static void lf_fill_common(LfArgs& a, const dip_layer_t* L, uint8_t* ws, const LfLayout& lay,
                            const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
                            dip_bf16* y, dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used) {
@@ -1364,7 +1427,8 @@ extern "C" int dip_mlp_decode_fused_tp(const dip_layer_t* shard, int64_t inter_t
                                        int world, void* const* workspaces, size_t workspace_bytes,
                                        const dip_bf16* x, const dip_bf16* resid, float eps,
                                        int64_t k, dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
-                                       dip_bf16* x_used, dip_stream_t stream) {
+                                       dip_bf16* x_used, const dip_fused_opts_t* opts,
+                                       dip_stream_t stream) {
   if (!shard || !x || !y || !workspaces) return DIP_ERR_ARG;
   if (world < 1 || world > kLfMaxRanks || rank < 0 || rank >= world) return DIP_ERR_ARG;
   const int64_t H = shard->hidden, I = shard->inter;
@@ -1392,6 +1456,7 @@ extern "C" int dip_mlp_decode_fused_tp(const dip_layer_t* shard, int64_t inter_t
   uint8_t* ws = static_cast<uint8_t*>(workspaces[rank]);
   lf_fill_common(a, shard, ws, lay, x, resid, eps, k, y, g_out, idx_out, x_used);
   a.idx = idx_out;  // optional: only this rank's entries are written
+  if (!lf_apply_opts(a, opts)) return DIP_ERR_ARG;
   a.inter_total = (int)inter_total;
   a.rank = rank;
   a.world = world;
@@ -1420,7 +1485,8 @@ extern "C" int dip_mlp_decode_fused_ex(const dip_layer_t* L, const dip_ca_cache_
                                        const dip_bf16* x, const dip_bf16* resid, float eps,
                                        int64_t k, void* workspace, size_t workspace_bytes,
                                        dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
-                                       dip_bf16* x_used, dip_bf16* h_out, dip_stream_t stream) {
+                                       dip_bf16* x_used, const dip_fused_opts_t* opts,
+                                       dip_stream_t stream) {
   if (!L || !x || !y || !workspace) return DIP_ERR_ARG;
   if (cache && (!cache->id2slot || !cache->res_up_qw || !cache->res_up_sc || !cache->res_dn_qw ||
                 !cache->res_dn_sc))
@@ -1443,7 +1509,7 @@ extern "C" int dip_mlp_decode_fused_ex(const dip_layer_t* L, const dip_ca_cache_
   LfArgs a = {};
   lf_fill_common(a, L, static_cast<uint8_t*>(workspace), lay, x, resid, eps, k, y, g_out, idx_out,
                  x_used);
-  a.h_out = h_out;
+  if (!lf_apply_opts(a, opts)) return DIP_ERR_ARG;
   a.err = error_word_ptr();
   if (!a.err) return DIP_ERR_CUDA;
   if (cache) {

@@ -518,11 +518,37 @@ Tensor gather_down_partial(const Tensor& dt_qw, const Tensor& dt_sc, const Tenso
   return y;
 }
 
+// Optional extras of a fused-layer call: h_out [h_len] bf16; the next
+// layer's gate weights (same shape as this layer's) for the L2 prefetch.
+dip_fused_opts_t make_opts(const std::optional<Tensor>& h_out, const std::optional<Tensor>& next_gq,
+                           const std::optional<Tensor>& next_gs, const Tensor& gate_qw,
+                           const Tensor& gate_sc, int64_t h_len) {
+  dip_fused_opts_t o = {nullptr, nullptr, nullptr};
+  if (h_out.has_value()) {
+    TORCH_CHECK(h_out->is_cuda() && h_out->is_contiguous() &&
+                    h_out->scalar_type() == at::kBFloat16 && h_out->numel() == h_len,
+                "h_out must be a contiguous CUDA bf16 tensor of ", h_len, " elements");
+    o.h_out = reinterpret_cast<dip_bf16*>(h_out->data_ptr());
+  }
+  TORCH_CHECK(next_gq.has_value() == next_gs.has_value(),
+              "next_gate_qw and next_gate_sc go together");
+  if (next_gq.has_value()) {
+    TORCH_CHECK(next_gq->is_cuda() && next_gq->is_contiguous() && next_gs->is_contiguous() &&
+                    next_gq->sizes() == gate_qw.sizes() && next_gs->sizes() == gate_sc.sizes(),
+                "next layer's gate weights must be contiguous CUDA tensors of this layer's shape");
+    o.prefetch_gate_qw = i8(*next_gq);
+    o.prefetch_gate_sc = bf(*next_gs);
+  }
+  return o;
+}
+
 std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
     const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
     const Tensor& dt_qw, const Tensor& dt_sc, const dip_ca_cache_t* cache, const Tensor& x_in,
     const std::optional<Tensor>& resid, double eps, int64_t k, const std::optional<Tensor>& ws_opt,
-    const std::optional<Tensor>& h_out = std::nullopt) {
+    const std::optional<Tensor>& h_out = std::nullopt,
+    const std::optional<Tensor>& next_gq = std::nullopt,
+    const std::optional<Tensor>& next_gs = std::nullopt) {
   check_packed(gate_qw, gate_sc, "mlp_decode_fused(gate)");
   check_packed(up_qw, up_sc, "mlp_decode_fused(up)");
   check_packed(dt_qw, dt_sc, "mlp_decode_fused(down_t)");
@@ -547,16 +573,10 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
   Tensor ws = ws_opt.has_value() ? *ws_opt : at::zeros({(int64_t)wsb}, x.options().dtype(at::kByte));
   TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && (size_t)ws.nbytes() >= wsb,
               "mlp_decode_fused: workspace too small (need ", wsb, " bytes)");
-  dip_bf16* hp = nullptr;
-  if (h_out.has_value()) {
-    TORCH_CHECK(h_out->is_cuda() && h_out->is_contiguous() &&
-                    h_out->scalar_type() == at::kBFloat16 && h_out->numel() == inter,
-                "mlp_decode_fused: h_out must be a contiguous CUDA bf16 [inter] tensor");
-    hp = reinterpret_cast<dip_bf16*>(h_out->data_ptr());
-  }
+  const dip_fused_opts_t opts = make_opts(h_out, next_gq, next_gs, gate_qw, gate_sc, inter);
   check_status(dip_mlp_decode_fused_ex(&L, cache, bf(x), resid.has_value() ? bf(r) : nullptr,
                                        (float)eps, k, ws.data_ptr(), wsb, bfm(y), bfm(g),
-                                       idx.data_ptr<int32_t>(), nullptr, hp, cur_stream()),
+                                       idx.data_ptr<int32_t>(), nullptr, &opts, cur_stream()),
                "mlp_decode_fused");
   return {y, g, idx};
 }
@@ -564,9 +584,10 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_impl(
 std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused(
     const Tensor& gate_qw, const Tensor& gate_sc, const Tensor& up_qw, const Tensor& up_sc,
     const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
-    double eps, int64_t k, const std::optional<Tensor>& ws_opt, const std::optional<Tensor>& h_out) {
+    double eps, int64_t k, const std::optional<Tensor>& ws_opt, const std::optional<Tensor>& h_out,
+    const std::optional<Tensor>& next_gq, const std::optional<Tensor>& next_gs) {
   return mlp_decode_fused_impl(gate_qw, gate_sc, up_qw, up_sc, dt_qw, dt_sc, nullptr, x_in, resid,
-                               eps, k, ws_opt, h_out);
+                               eps, k, ws_opt, h_out, next_gq, next_gs);
 }
 
 // the cache-aware layer in one launch (dip_mlp_decode_fused_ca)
@@ -575,7 +596,8 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_ca(
     const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& id2slot, const Tensor& res_up_qw,
     const Tensor& res_up_sc, const Tensor& res_dn_qw, const Tensor& res_dn_sc, const Tensor& x_in,
     const std::optional<Tensor>& resid, double eps, int64_t k,
-    const std::optional<Tensor>& ws_opt) {
+    const std::optional<Tensor>& ws_opt, const std::optional<Tensor>& next_gq,
+    const std::optional<Tensor>& next_gs) {
   TORCH_CHECK(id2slot.is_cuda() && id2slot.scalar_type() == at::kLong && id2slot.is_contiguous() &&
                   id2slot.numel() == gate_qw.size(0),
               "mlp_decode_fused_ca: id2slot must be a contiguous CUDA int64 [inter] tensor");
@@ -587,7 +609,7 @@ std::tuple<Tensor, Tensor, Tensor> mlp_decode_fused_ca(
   dip_ca_cache_t c = {id2slot.data_ptr<int64_t>(), i8(res_up_qw), bf(res_up_sc), i8(res_dn_qw),
                       bf(res_dn_sc), res_up_qw.size(0)};
   return mlp_decode_fused_impl(gate_qw, gate_sc, up_qw, up_sc, dt_qw, dt_sc, &c, x_in, resid, eps,
-                               k, ws_opt);
+                               k, ws_opt, std::nullopt, next_gq, next_gs);
 }
 
 // one tensor-parallel layer on this rank (dip_mlp_decode_fused_tp); the
@@ -597,7 +619,8 @@ std::tuple<Tensor, Tensor> mlp_decode_fused_tp(
     const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& x_in, const std::optional<Tensor>& resid,
     double eps, int64_t k, int64_t inter_total, int64_t rank, int64_t world,
     at::IntArrayRef workspaces, int64_t workspace_bytes, const std::optional<Tensor>& idx_out,
-    const std::optional<Tensor>& x_used) {
+    const std::optional<Tensor>& x_used, const std::optional<Tensor>& h_out,
+    const std::optional<Tensor>& next_gq, const std::optional<Tensor>& next_gs) {
   check_packed(gate_qw, gate_sc, "mlp_decode_fused_tp(gate)");
   check_packed(up_qw, up_sc, "mlp_decode_fused_tp(up)");
   check_packed(dt_qw, dt_sc, "mlp_decode_fused_tp(down_t)");
@@ -634,10 +657,11 @@ std::tuple<Tensor, Tensor> mlp_decode_fused_tp(
   std::vector<void*> ws(workspaces.size());
   for (size_t q = 0; q < ws.size(); ++q) ws[q] = reinterpret_cast<void*>(workspaces[q]);
   Tensor y = bf16_empty(hidden, x), g = bf16_empty(inter, x);
+  const dip_fused_opts_t opts = make_opts(h_out, next_gq, next_gs, gate_qw, gate_sc, inter_total);
   check_status(dip_mlp_decode_fused_tp(&L, inter_total, (int)rank, (int)world, ws.data(),
                                        (size_t)workspace_bytes, bf(x),
                                        resid.has_value() ? bf(r) : nullptr, (float)eps, k, bfm(y),
-                                       bfm(g), idxp, xu, cur_stream()),
+                                       bfm(g), idxp, xu, &opts, cur_stream()),
                "mlp_decode_fused_tp");
   return {y, g};
 }
@@ -711,20 +735,23 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def(
       "mlp_decode_fused(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
       "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
-      "Tensor? workspace=None, Tensor? h_out=None) -> (Tensor, Tensor, Tensor)");
+      "Tensor? workspace=None, Tensor? h_out=None, Tensor? next_gate_qw=None, "
+      "Tensor? next_gate_sc=None) -> (Tensor, Tensor, Tensor)");
   m.def("mlp_fused_workspace_bytes(int hidden, int inter, int k) -> int");
   m.def(
       "mlp_decode_fused_tp(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
       "Tensor down_t_qw, Tensor down_t_sc, Tensor x, Tensor? resid, float eps, int k, "
       "int inter_total, int rank, int world, int[] workspaces, int workspace_bytes, "
-      "Tensor? idx_out=None, Tensor? x_used=None) -> (Tensor, Tensor)");
+      "Tensor? idx_out=None, Tensor? x_used=None, Tensor? h_out=None, "
+      "Tensor? next_gate_qw=None, Tensor? next_gate_sc=None) -> (Tensor, Tensor)");
   m.def("mlp_fused_tp_workspace_bytes(int hidden, int inter_total, int k) -> int");
   m.def("set_spin_limit(int polls) -> int");
   m.def(
       "mlp_decode_fused_ca(Tensor gate_qw, Tensor gate_sc, Tensor up_qw, Tensor up_sc, "
       "Tensor down_t_qw, Tensor down_t_sc, Tensor id2slot, Tensor res_up_qw, Tensor res_up_sc, "
       "Tensor res_dn_qw, Tensor res_dn_sc, Tensor x, Tensor? resid, float eps, int k, "
-      "Tensor? workspace=None) -> (Tensor, Tensor, Tensor)");
+      "Tensor? workspace=None, Tensor? next_gate_qw=None, Tensor? next_gate_sc=None) "
+      "-> (Tensor, Tensor, Tensor)");
   m.def("quantize_int4(Tensor w) -> (Tensor, Tensor)");
   m.def("dequantize_int4(Tensor qweight, Tensor scales) -> Tensor");
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");

@@ -103,21 +103,24 @@ def _register_fakes() -> None:
 
 def _register_fakes_fused():
     @torch.library.register_fake("dip_b200::mlp_decode_fused")
-    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, workspace=None, h_out=None):
+    def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, workspace=None, h_out=None,
+          next_gate_qw=None, next_gate_sc=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))
 
 
     @torch.library.register_fake("dip_b200::mlp_decode_fused_ca")
-    def _(gq, gs, uq, us, dq, ds, id2slot, ruq, rus, rdq, rds, x, resid, eps, k, workspace=None):
+    def _(gq, gs, uq, us, dq, ds, id2slot, ruq, rus, rdq, rds, x, resid, eps, k, workspace=None,
+          next_gate_qw=None, next_gate_sc=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device),
                 torch.empty(k, dtype=torch.int32, device=x.device))
 
     @torch.library.register_fake("dip_b200::mlp_decode_fused_tp")
     def _(gq, gs, uq, us, dq, ds, x, resid, eps, k, inter_total, rank, world, workspaces,
-          workspace_bytes, idx_out=None, x_used=None):
+          workspace_bytes, idx_out=None, x_used=None, h_out=None, next_gate_qw=None,
+          next_gate_sc=None):
         return (torch.empty(gq.shape[1] * 2, dtype=torch.bfloat16, device=x.device),
                 torch.empty(gq.shape[0], dtype=torch.bfloat16, device=x.device))
 

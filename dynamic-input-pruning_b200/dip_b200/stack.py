@@ -168,18 +168,23 @@ class DipStack:
         idxs, splits, ys = [], [], []
         y = None
         for l, L in enumerate(self.layers):
+            # the next layer's gate rows (layer 0's after the last layer: the
+            # next token) are moved into L2 during this layer's tail
+            nxt = self.layers[(l + 1) % len(self.layers)]
             if self.mode == "fused":
                 xin, r = (x0, None) if l == 0 else (y, resid[l])
                 y, g, idx = torch.ops.dip_b200.mlp_decode_fused(
                     L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
-                    L["down_t_sc"], xin, r, RMS_EPS, k, self._ws)
+                    L["down_t_sc"], xin, r, RMS_EPS, k, self._ws, None, nxt["gate_qw"],
+                    nxt["gate_sc"])
             elif self.mode == "ca":
                 C = self.ca[l]
                 xin, r = (x0, None) if l == 0 else (y, resid[l])
                 y, g, idx = torch.ops.dip_b200.mlp_decode_fused_ca(
                     L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], L["down_t_qw"],
                     L["down_t_sc"], C["id2slot"], C["res_up_qw"], C["res_up_sc"],
-                    C["res_dn_qw"], C["res_dn_sc"], xin, r, RMS_EPS, k, self._ws)
+                    C["res_dn_qw"], C["res_dn_sc"], xin, r, RMS_EPS, k, self._ws, nxt["gate_qw"],
+                    nxt["gate_sc"])
                 if record:
                     splits.append(torch.ops.dip_b200.ca_split(idx, C["id2slot"]))
             else:

@@ -342,10 +342,11 @@ class TPFusedStack:
             if record:
                 idx = torch.zeros(cfg.k, dtype=torch.int32, device=self.device)
                 xu = torch.empty(cfg.hidden, dtype=torch.bfloat16, device=self.device)
+            nxt = self.shards[(l + 1) % len(self.shards)]
             y, _ = torch.ops.dip_b200.mlp_decode_fused_tp(
                 s["gate_qw"], s["gate_sc"], s["up_qw"], s["up_sc"], s["down_t_qw"],
                 s["down_t_sc"], xin, r, RMS_EPS, cfg.k, cfg.inter, self.rank, self.world,
-                ws.ptrs, ws.nbytes, idx, xu)
+                ws.ptrs, ws.nbytes, idx, xu, None, nxt["gate_qw"], nxt["gate_sc"])
             if record:
                 idxs.append(idx)
                 xs.append(xu)

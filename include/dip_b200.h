@@ -264,16 +264,27 @@ DIP_API int dip_mlp_decode_fused_ca(const dip_layer_t* layer, const dip_ca_cache
                                     void* workspace, size_t workspace_bytes, dip_bf16* y,
                                     dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
                                     dip_stream_t stream);
-/* As dip_mlp_decode_fused_ca, plus h_out (optional, [inter] bf16): for every
- * selected channel c, h_out[c] = bf16(g[c] * bf16(u[c])), the h_sel of
- * dip_stream_predispatch.py:201 that the down projection consumes (entries
- * of unselected channels are left untouched).  Lets a caller check the up
- * stage and the down stage of the one-launch layer separately. */
+/* Optional extras of a fused-layer call (any field may be NULL).
+ *   h_out [inter] bf16: for every selected channel c, h_out[c] =
+ *     bf16(g[c] * bf16(u[c])), the h_sel of dip_stream_predispatch.py:201
+ *     that the down projection consumes (other entries untouched); lets a
+ *     caller check the up stage and the down stage separately.
+ *   prefetch_gate_qw / prefetch_gate_sc: the NEXT layer's gate weights (same
+ *     shape as this layer's, 16-byte aligned, both or neither).  Once a worker
+ *     SM has finished its own rows it moves the first rows of the same range
+ *     of those weights into L2, so the next call's first tiles come from L2.
+ *     A hint only: results do not depend on it. */
+typedef struct {
+  dip_bf16* h_out;
+  const int8_t* prefetch_gate_qw;
+  const dip_bf16* prefetch_gate_sc;
+} dip_fused_opts_t;
+/* As dip_mlp_decode_fused_ca, with the extras of `opts` (may be NULL). */
 DIP_API int dip_mlp_decode_fused_ex(const dip_layer_t* layer, const dip_ca_cache_t* cache,
                                     const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
                                     void* workspace, size_t workspace_bytes, dip_bf16* y,
                                     dip_bf16* g_out, int32_t* idx_out, dip_bf16* x_used,
-                                    dip_bf16* h_out, dip_stream_t stream);
+                                    const dip_fused_opts_t* opts, dip_stream_t stream);
 
 /* ---- batched decode and dense forward on tcgen05 tensor cores ------------------
  * The reference decode path is batch-1 (dip_stream_predispatch.py:170, :182); a
@@ -362,6 +373,8 @@ DIP_API int dip_p2p_reduce(int rank, int world, void* const* mailboxes, const fl
  * (dip_mlp_fused_tp_workspace_bytes, zeroed before the first call, 256-byte
  * aligned; peers' mapped through dip_ipc_open).  Every rank makes the same
  * sequence of calls with the same shapes on GPUs with the same SM count.
+ * opts as for dip_mlp_decode_fused_ex (h_out indexed by global channel id;
+ * prefetch: the next layer's shard).
  * idx_out (optional, [k]) receives only the entries of this rank's channels
  * (global channel ids at their global positions; rank 0 also writes the zero
  * padding); g_out (optional) this rank's g slice.  Waits are bounded (device
@@ -372,7 +385,8 @@ DIP_API int dip_mlp_decode_fused_tp(const dip_layer_t* shard, int64_t inter_tota
                                     int world, void* const* workspaces, size_t workspace_bytes,
                                     const dip_bf16* x, const dip_bf16* resid, float eps, int64_t k,
                                     dip_bf16* y, dip_bf16* g_out, int32_t* idx_out,
-                                    dip_bf16* x_used, dip_stream_t stream);
+                                    dip_bf16* x_used, const dip_fused_opts_t* opts,
+                                    dip_stream_t stream);
 
 /* ---- a1/a3: weight format ---------------------------------------------------------
  * Symmetric int4 group-128 quantisation of a bf16 [rows, cols] matrix, bit
