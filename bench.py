@@ -380,7 +380,10 @@ def run_config3(args, emit=True):
     """Config 3: B independent tokens per step through the 64-layer stack
     (per-token DIP selection; `--path tc` (default) streams every weight once
     for the batch through the tcgen05 GEMMs, `--path gather` gathers each
-    token's rows).  `value` is tokens per second of the whole batch."""
+    token's rows).  `value` is tokens per second of the whole batch.  Under
+    torchrun with N > 1 ranks: config 4 at batch B (run_tp_batch)."""
+    if dist_env()[1] > 1:
+        return run_tp_batch(args)
     import dip_b200  # noqa: F401
     from dip_b200.stack import StackConfig, layer_weight_bytes
     from dip_b200.batch import BatchedDipStack
@@ -435,6 +438,69 @@ def run_config3(args, emit=True):
     if emit:
         print(json.dumps(rec), flush=True)
     return rec
+
+
+def run_tp_batch(args):
+    """Config 4 at batch B (`--config 3 --batch B` under torchrun): the
+    batched stack sharded along I (TPBatchedDipStack: tcgen05 GEMMs on each
+    rank's rows, NCCL all-gather of g and all-reduce of the fp32 partials).
+    After the timed steps rank 0 checks one step's per-token indices at every
+    layer against the single-GPU batched layer on the full weights and the
+    same inputs (tp_idx_exact)."""
+    rank, world, local = dist_env()
+    import torch.distributed as dist
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, layer_weight_bytes
+    from dip_b200.batch import batched_dip_layer
+    from dip_b200.tp import TPBatchedDipStack
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    B = args.batch
+    cfg = StackConfig(n_layers=args.layers, seed=0)
+    stack = TPBatchedDipStack(cfg, B, dev, keep_full=(rank == 0))
+    T = args.warmup + args.steps
+    gen = torch.Generator().manual_seed(3000)
+    x0 = torch.randn(T, B, cfg.hidden, generator=gen).to(torch.bfloat16).to(dev)
+    resid = torch.randn(T, cfg.n_layers, B, cfg.hidden, generator=gen).to(torch.bfloat16).to(dev)
+    ms, clk = _timed_replays(stack, x0, resid, args.warmup, args.steps, dev, world)
+    if _device_error_all(world, dev):
+        raise SystemExit("a bounded device wait ran out during the timed steps: run invalid")
+    stack.step(x0[args.warmup], resid[args.warmup], record=True)
+    torch.cuda.synchronize()
+    n_bad = 0
+    if rank == 0:
+        for l in range(cfg.n_layers):
+            _, _, idx1 = batched_dip_layer(stack.full[l], stack.last_x[l], cfg.k, "tc")
+            n_bad += int(not torch.equal(idx1, stack.last_idx[l]))
+    flag = torch.tensor([n_bad], device=dev)
+    dist.broadcast(flag, 0)
+    n_bad = int(flag.item())
+    nb = layer_weight_bytes(cfg)
+    layer_us = ms * 1e3 / cfg.n_layers
+    per_gpu = nb["gate"] * 3 // world
+    peak, peak_kind = _peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": B * 1e3 / ms, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) int4 g128 weights, N(0,1) tokens)",
+            "config": {"workload": f"config4: the batch-{B} stack sharded along I over "
+                                   f"{world} GPUs", "batch": B, "layers": cfg.n_layers,
+                       "k": cfg.k, "parallelism": f"tp{world}", "path": "tc"},
+            "us_per_layer": layer_us, "us_per_token_layer": layer_us / B,
+            "per_gpu_hbm_gbs": per_gpu / (layer_us * 1e-6) / 1e9,
+            "per_gpu_hbm_frac_of_measured": per_gpu / (layer_us * 1e-6) / 1e9 / peak,
+            "peak_kind": peak_kind,
+            "tp_idx_exact": n_bad == 0, "tp_idx_layers_checked": cfg.n_layers,
+            "tp_idx_layers_differing": n_bad,
+            "gpu_launches": args.steps * cfg.n_layers * 9,
+            "clocks": clk}), flush=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    sys.stdout.flush()
+    os._exit(0 if n_bad == 0 else 3)
 
 
 def _barrier(world):

@@ -673,10 +673,26 @@ extern "C" size_t dip_int4_gemm_tc_workspace_bytes(int64_t rows, int64_t in_feat
          (size_t)kTcMaxSplitRows * batch * rows * sizeof(float);
 }
 
+extern "C" int dip_int4_gemm_tc_auto_split(int64_t rows, int64_t in_features) {
+  if (rows <= 0 || in_features <= 0 || in_features % kTcChunkK) return 0;
+  return tc_pick_split((int)((rows + kTcM - 1) / kTcM), (int)(in_features / kTcChunkK),
+                       kTcMaxSplitRows);
+}
+
 extern "C" int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, const dip_bf16* x,
                                 int64_t rows, int64_t in_features, int64_t batch, int epilogue,
                                 const dip_bf16* g, const uint32_t* sel_count, void* workspace,
                                 size_t workspace_bytes, dip_bf16* out, dip_stream_t stream) {
+  return dip_int4_gemm_tc_split(qweight, scales, x, rows, in_features, batch, epilogue, g,
+                                sel_count, 0, workspace, workspace_bytes, out, stream);
+}
+
+extern "C" int dip_int4_gemm_tc_split(const int8_t* qweight, const dip_bf16* scales,
+                                      const dip_bf16* x, int64_t rows, int64_t in_features,
+                                      int64_t batch, int epilogue, const dip_bf16* g,
+                                      const uint32_t* sel_count, int ksplit, void* workspace,
+                                      size_t workspace_bytes, dip_bf16* out, dip_stream_t stream) {
+  if (ksplit < 0 || ksplit > kTcMaxSplitRows) return DIP_ERR_ARG;
   int rc = tc_check_rows(qweight, scales, x, rows, in_features, batch);
   if (rc) return rc;
   if (!out || !workspace) return DIP_ERR_ARG;
@@ -697,7 +713,10 @@ extern "C" int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, c
   a.K = (int)in_features;
   a.B = (int)batch;
   a.kgran = kTcChunkK / kTcK;
-  a.ksplit = tc_pick_split((int)((rows + kTcM - 1) / kTcM), (int)(in_features / kTcChunkK), kTcMaxSplitRows);
+  a.ksplit = ksplit ? ksplit
+                   : tc_pick_split((int)((rows + kTcM - 1) / kTcM), (int)(in_features / kTcChunkK),
+                                   kTcMaxSplitRows);
+  if (a.ksplit > (int)(in_features / kTcChunkK)) return DIP_ERR_ARG;
   a.out = out;
   a.g = g;
   a.cnt = sel_count;
@@ -729,11 +748,46 @@ extern "C" size_t dip_int4_down_tc_workspace_bytes(int64_t out_features, int64_t
   return (size_t)8 * batch * out_features * sizeof(float);
 }
 
+namespace dip {
+static int down_tc_impl(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
+                        int64_t inter, int64_t out_features, int64_t batch, void* workspace,
+                        size_t workspace_bytes, dip_bf16* y, float* y_f32, dip_stream_t stream);
+}
+
 extern "C" int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
                                 int64_t inter, int64_t out_features, int64_t batch,
                                 void* workspace, size_t workspace_bytes, dip_bf16* y,
                                 dip_stream_t stream) {
-  if (!down_t || !scales || !h || !y || !workspace || inter <= 0 || out_features <= 0 ||
+  if (!y) return DIP_ERR_ARG;
+  return down_tc_impl(down_t, scales, h, inter, out_features, batch, workspace, workspace_bytes, y,
+                      nullptr, stream);
+}
+
+extern "C" int dip_int4_down_tc_f32(const int8_t* down_t, const dip_bf16* scales,
+                                    const dip_bf16* h, int64_t inter, int64_t out_features,
+                                    int64_t batch, void* workspace, size_t workspace_bytes,
+                                    float* y_f32, dip_stream_t stream) {
+  if (!y_f32) return DIP_ERR_ARG;
+  return down_tc_impl(down_t, scales, h, inter, out_features, batch, workspace, workspace_bytes,
+                      nullptr, y_f32, stream);
+}
+
+namespace dip {
+__global__ void tc_reduce_f32_kernel(const float* __restrict__ part, int ksplit, int64_t n,
+                                     float* __restrict__ y) {
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int p = 0; p < ksplit; ++p) s += part[p * n + i];
+    y[i] = s;
+  }
+}
+
+static int down_tc_impl(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
+                        int64_t inter, int64_t out_features, int64_t batch, void* workspace,
+                        size_t workspace_bytes, dip_bf16* y, float* y_f32, dip_stream_t stream) {
+  if (!down_t || !scales || !h || !workspace || inter <= 0 || out_features <= 0 ||
       batch <= 0 || batch > kTcMaxN)
     return DIP_ERR_ARG;
   if (inter % kTcK != 0 || out_features % 256 != 0 || inter > (1 << 24)) return DIP_ERR_UNSUPPORTED;
@@ -760,10 +814,15 @@ extern "C" int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, co
   int rc = tc_launch<kTcEpiF32, true>(a, st);
   if (rc) return rc;
   const int64_t n = batch * out_features;
-  return launch_status(launch(tc_reduce_kernel, dim3((unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184)),
-                              dim3(256), 0, st, (const float*)a.out_f32, ks, n, (int)kTcEpiBf16,
-                              (const uint16_t*)nullptr, (const uint32_t*)nullptr, y));
+  const dim3 grid((unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184));
+  if (y_f32)
+    return launch_status(launch(tc_reduce_f32_kernel, grid, dim3(256), 0, st,
+                                (const float*)a.out_f32, ks, n, y_f32));
+  return launch_status(launch(tc_reduce_kernel, grid, dim3(256), 0, st, (const float*)a.out_f32, ks,
+                              n, (int)kTcEpiBf16, (const uint16_t*)nullptr,
+                              (const uint32_t*)nullptr, y));
 }
+}  // namespace dip
 
 namespace dip {
 // cnt[b][c] = number of times channel c appears in idx[b] (zeroed first by the host).

@@ -386,7 +386,8 @@ Tensor residual_rmsnorm(const Tensor& y_in, const Tensor& r_in, double eps) {
 
 // batched decode / dense forward on tcgen05: x [B, in] -> [B, rows]
 Tensor gemm_tc(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, int64_t epilogue,
-               const c10::optional<Tensor>& g_in, const c10::optional<Tensor>& cnt_in) {
+               const c10::optional<Tensor>& g_in, const c10::optional<Tensor>& cnt_in,
+               int64_t ksplit) {
   check_packed(qweight, scales, "gemm_tc");
   Tensor x = x_in.contiguous();
   check_cuda(x, "x");
@@ -410,10 +411,34 @@ Tensor gemm_tc(const Tensor& qweight, const Tensor& scales, const Tensor& x_in, 
   }
   const size_t nws = dip_int4_gemm_tc_workspace_bytes(qweight.size(0), x.size(1), x.size(0));
   Tensor ws = at::empty({(int64_t)nws}, x.options().dtype(at::kByte));
-  check_status(dip_int4_gemm_tc(i8(qweight), bf(scales), bf(x), qweight.size(0), x.size(1), x.size(0),
-                                (int)epilogue, gp, cp, ws.data_ptr(), nws, bfm(out), cur_stream()),
+  check_status(dip_int4_gemm_tc_split(i8(qweight), bf(scales), bf(x), qweight.size(0), x.size(1),
+                                      x.size(0), (int)epilogue, gp, cp, (int)ksplit, ws.data_ptr(),
+                                      nws, bfm(out), cur_stream()),
                "gemm_tc");
   return out;
+}
+
+// h [B, inter] -> fp32 y [B, hidden] (a tensor-parallel partial)
+Tensor down_tc_f32(const Tensor& dt_qw, const Tensor& dt_sc, const Tensor& h_in) {
+  check_packed(dt_qw, dt_sc, "down_tc_f32");
+  Tensor h = h_in.contiguous();
+  check_cuda(h, "h");
+  check_dtype(h, at::kBFloat16, "h");
+  TORCH_CHECK(h.dim() == 2 && h.size(1) == dt_qw.size(0), "down_tc_f32: h must be [B, inter]");
+  c10::cuda::CUDAGuard guard(h.device());
+  const int64_t out_f = dt_qw.size(1) * 2, B = h.size(0);
+  Tensor y = at::empty({B, out_f}, h.options().dtype(at::kFloat));
+  if (B == 0) return y;
+  const size_t nws = dip_int4_down_tc_workspace_bytes(out_f, B);
+  Tensor ws = at::empty({(int64_t)nws}, h.options().dtype(at::kByte));
+  check_status(dip_int4_down_tc_f32(i8(dt_qw), bf(dt_sc), bf(h), dt_qw.size(0), out_f, B,
+                                    ws.data_ptr(), nws, y.data_ptr<float>(), cur_stream()),
+               "down_tc_f32");
+  return y;
+}
+
+int64_t op_gemm_tc_auto_split(int64_t rows, int64_t in_features) {
+  return dip_int4_gemm_tc_auto_split(rows, in_features);
 }
 
 // h [B, inter] -> y [B, hidden] over the transposed down weights
@@ -757,7 +782,9 @@ TORCH_LIBRARY(dip_b200, m) {
   m.def("transpose_down_int4(Tensor down_qw, Tensor down_sc) -> (Tensor, Tensor)");
   m.def("residual_rmsnorm(Tensor y, Tensor r, float eps) -> Tensor");
   m.def("gemv_batched(Tensor qweight, Tensor scales, Tensor x, bool silu) -> Tensor");
-  m.def("gemm_tc(Tensor qweight, Tensor scales, Tensor x, int epilogue, Tensor? g=None, Tensor? cnt=None) -> Tensor");
+  m.def("gemm_tc(Tensor qweight, Tensor scales, Tensor x, int epilogue, Tensor? g=None, Tensor? cnt=None, int ksplit=0) -> Tensor");
+  m.def("down_tc_f32(Tensor down_t_qw, Tensor down_t_sc, Tensor h) -> Tensor");
+  m.def("gemm_tc_auto_split(int rows, int in_features) -> int");
   m.def("down_tc(Tensor down_t_qw, Tensor down_t_sc, Tensor h) -> Tensor");
   m.def("select_count(Tensor idx, int inter) -> Tensor");
   m.def("shard_select(Tensor idx, int lo, int hi) -> (Tensor, Tensor)");
@@ -790,6 +817,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CUDA, m) {
   m.impl("gemv_batched", &gemv_batched);
   m.impl("gemm_tc", &gemm_tc);
   m.impl("down_tc", &down_tc);
+  m.impl("down_tc_f32", &down_tc_f32);
   m.impl("select_count", &select_count);
   m.impl("shard_select", &shard_select);
   m.impl("gather_up_h_count", &gather_up_h_count);
@@ -801,6 +829,7 @@ TORCH_LIBRARY_IMPL(dip_b200, CompositeExplicitAutograd, m) {
   m.impl("mlp_fused_workspace_bytes", &op_mlp_fused_workspace_bytes);
   m.impl("mlp_fused_tp_workspace_bytes", &op_mlp_fused_tp_workspace_bytes);
   m.impl("set_spin_limit", &op_set_spin_limit);
+  m.impl("gemm_tc_auto_split", &op_gemm_tc_auto_split);
   m.impl("set_gemv_variant", &op_set_gemv_variant);
   m.impl("take_device_error", &op_take_device_error);
 }

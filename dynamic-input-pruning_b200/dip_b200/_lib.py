@@ -128,8 +128,12 @@ def _register_fakes_fused():
     def _(qweight, scales, x, silu):
         return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)
 
+    @torch.library.register_fake("dip_b200::down_tc_f32")
+    def _(dt_qw, dt_sc, h):
+        return torch.empty(h.shape[0], dt_qw.shape[1] * 2, dtype=torch.float32, device=h.device)
+
     @torch.library.register_fake("dip_b200::gemm_tc")
-    def _(qweight, scales, x, epilogue, g=None, cnt=None):
+    def _(qweight, scales, x, epilogue, g=None, cnt=None, ksplit=0):
         return torch.empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16, device=x.device)
 
     @torch.library.register_fake("dip_b200::down_tc")

@@ -391,3 +391,85 @@ class TPFusedStack:
             torch.cuda.current_stream(self.device).synchronize()
             return res
         return out
+
+
+class TPBatchedDipStack:
+    """Config 4 at batch B: the batched stack (dip_b200.batch, tcgen05 path)
+    with every layer sharded along I.  Per layer and rank:
+
+      g_loc = GEMM(gate shard, x) with the full layer's K split   [B, I/P]
+      g     = all-gather of g_loc (NCCL)                          [B, I]
+      idx   = per-token top-k of |g| (the same on every rank)     [B, k]
+      h_loc = GEMM(up shard, x), epilogue h * count of the rank's channels
+      y_loc = fp32 down projection of h_loc                       [B, H]
+      y     = bf16(all-reduce sum of y_loc) (NCCL)
+
+    Every gate row is computed with the same K ranges as the unsharded GEMM,
+    so g and the indices are bit-identical to one GPU's; y agrees up to the
+    order of the fp32 sums.  keep_full keeps the unsharded weights (the
+    in-run check)."""
+
+    def __init__(self, cfg, batch: int, device, group=None, keep_full: bool = False):
+        from .stack import make_layer
+        self.cfg, self.batch = cfg, batch
+        self.device = torch.device(device)
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.lo, self.hi = shard_range(cfg.inter, self.rank, self.world)
+        self.ksplit = int(torch.ops.dip_b200.gemm_tc_auto_split(cfg.inter, cfg.hidden))
+        self.shards, self.full = [], [] if keep_full else None
+        for l in range(cfg.n_layers):
+            full = make_layer(cfg, l, self.device)
+            self.shards.append(shard_layer(full, self.rank, self.world))
+            if keep_full:
+                self.full.append(full)
+            del full
+        torch.cuda.empty_cache()
+        self._graph = self._static_in = self._static_out = None
+        self.last_idx = self.last_x = None
+
+    def layer(self, s, x):
+        B, I, P = x.shape[0], self.cfg.inter, self.world
+        g_loc = torch.ops.dip_b200.gemm_tc(s["gate_qw"], s["gate_sc"], x, 1, None, None,
+                                           self.ksplit)
+        parts = torch.empty(P, B, I // P, dtype=g_loc.dtype, device=x.device)
+        dist.all_gather_into_tensor(parts, g_loc.contiguous(), group=self.group)
+        g = parts.permute(1, 0, 2).reshape(B, I)
+        idx = torch.ops.dip_b200.topk_select_batched(g, self.cfg.k)
+        cnt = torch.ops.dip_b200.select_count(idx, I)[:, self.lo:self.hi].contiguous()
+        h = torch.ops.dip_b200.gemm_tc(s["up_qw"], s["up_sc"], x, 2, g_loc, cnt, self.ksplit)
+        y = torch.ops.dip_b200.down_tc_f32(s["down_t_qw"], s["down_t_sc"], h)
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y.to(torch.bfloat16), idx
+
+    def step(self, x0, resid, record=False):
+        from .stack import RMS_EPS
+        y, idxs, xs = None, [], []
+        for l, s in enumerate(self.shards):
+            x = x0 if l == 0 else torch.ops.dip_b200.residual_rmsnorm(y, resid[l], RMS_EPS)
+            y, idx = self.layer(s, x)
+            if record:
+                idxs.append(idx)
+                xs.append(x)
+        if record:
+            self.last_idx, self.last_x = idxs, xs
+        return y
+
+    def capture(self):
+        B, H, n = self.batch, self.cfg.hidden, self.cfg.n_layers
+        self._static_in = (torch.zeros(B, H, dtype=torch.bfloat16, device=self.device),
+                           torch.zeros(n, B, H, dtype=torch.bfloat16, device=self.device))
+        st = torch.cuda.Stream(device=self.device)
+        st.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(st):
+            for _ in range(2):
+                self.step(*self._static_in)
+        torch.cuda.current_stream(self.device).wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            self._static_out = self.step(*self._static_in)
+        self._graph = gr
+
+    def replay(self):
+        self._graph.replay()
+        return self._static_out

@@ -317,10 +317,30 @@ DIP_API int dip_int4_gemm_tc(const int8_t* qweight, const dip_bf16* scales, cons
  * int4_gather_down, int4_gather_down.cu:41-95).  Channels are split over the
  * SMs; the fp32 partials (workspace, dip_int4_down_tc_workspace_bytes) are
  * summed in a fixed order.  out a multiple of 256, inter of 64. */
+/* As dip_int4_gemm_tc with the number of K ranges fixed (ksplit 1..4; 0 =
+ * automatic).  Each K range's partial is summed in a fixed order, so two
+ * calls with the same ksplit compute every output row with the same
+ * summation order whatever the number of rows: a tensor-parallel shard of
+ * the gate passes the full layer's automatic choice
+ * (dip_int4_gemm_tc_auto_split(full rows, in_features)) and gets rows
+ * bit-identical to the unsharded GEMM.  No counterpart in the reference. */
+DIP_API int dip_int4_gemm_tc_auto_split(int64_t rows, int64_t in_features);
+DIP_API int dip_int4_gemm_tc_split(const int8_t* qweight, const dip_bf16* scales,
+                                   const dip_bf16* x, int64_t rows, int64_t in_features,
+                                   int64_t batch, int epilogue, const dip_bf16* g,
+                                   const uint32_t* sel_count, int ksplit, void* workspace,
+                                   size_t workspace_bytes, dip_bf16* out, dip_stream_t stream);
 DIP_API size_t dip_int4_down_tc_workspace_bytes(int64_t out_features, int64_t batch);
 DIP_API int dip_int4_down_tc(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
                              int64_t inter, int64_t out_features, int64_t batch, void* workspace,
                              size_t workspace_bytes, dip_bf16* y, dip_stream_t stream);
+/* As dip_int4_down_tc with the fp32 sums as output (y_f32 [batch, out]):
+ * a tensor-parallel shard's partial, summed over the ranks before the one
+ * bf16 rounding.  No counterpart in the reference. */
+DIP_API int dip_int4_down_tc_f32(const int8_t* down_t, const dip_bf16* scales, const dip_bf16* h,
+                                 int64_t inter, int64_t out_features, int64_t batch,
+                                 void* workspace, size_t workspace_bytes, float* y_f32,
+                                 dip_stream_t stream);
 /* cnt[b][c] = how many times channel c occurs in idx[b] (idx [batch, k]), the
  * selection of each token as dense counts for dip_int4_gemm_tc's epilogue 2
  * (the reference's index_select over idx, dip_stream_predispatch.py:199-203). */
