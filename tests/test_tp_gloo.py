@@ -98,8 +98,13 @@ def _dead_worker(rank, world, port, q):
     import datetime
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=5))
+    # the timeout also bounds the rendezvous: generous enough for a loaded host
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=15))
+    except Exception as e:
+        q.put((rank, "init failed:" + type(e).__name__))
+        return
     if rank == 1:
         q.put((rank, "left"))
         return  # exits without joining the all-gather
