@@ -196,6 +196,54 @@ def run_single_layer(n):
     print(json.dumps({"single_layer_launches": n, "y_abs_sum": float(y.float().abs().sum())}))
 
 
+def run_gemm_tc(n):
+    """n launches of the batch-64 gate GEMM (tcgen05, SiLU epilogue) on one
+    config-1 layer: the small fixed case for ncu captures of gemm_tc_kernel."""
+    import dip_b200  # noqa: F401
+    from dip_b200.stack import StackConfig, make_layer
+    dev = torch.device("cuda", 0)
+    cfg = StackConfig(n_layers=1, seed=0)
+    L = make_layer(cfg, 0, dev)
+    x = torch.randn(64, cfg.hidden, generator=torch.Generator().manual_seed(1))
+    x = x.to(torch.bfloat16).to(dev)
+    for _ in range(n):
+        g = torch.ops.dip_b200.gemm_tc(L["gate_qw"], L["gate_sc"], x, 1)
+    torch.cuda.synchronize()
+    assert torch.ops.dip_b200.take_device_error() == 0
+    print(json.dumps({"gemm_tc_launches": n, "g_abs_sum": float(g.float().abs().sum())}))
+
+
+def _module_forward_us(dev, reps=20):
+    """Config 0 through the drop-in module: StreamingDIPMlp(...)(x) with x
+    [1, 1, 5120], eager calls (Python, output allocation and the one fused
+    launch each), CUDA events around `reps` calls after warm-up."""
+    import dip_b200
+    from dip_b200.stack import StackConfig, make_layer
+    cfg = StackConfig(n_layers=1, seed=0)
+    L = make_layer(cfg, 0, dev)
+    # the module takes the untransposed down projection, as the reference does
+    gen = torch.Generator(device=dev).manual_seed(7)
+    wd = (torch.randn(cfg.hidden, cfg.inter, generator=gen, device=dev) * cfg.std)
+    dq, ds = torch.ops.dip_b200.quantize_int4(wd.to(torch.bfloat16))
+    del wd
+    shared = dip_b200.SharedBuffers(cfg.k, cfg.hidden // 2, cfg.hidden // 128, cfg.hidden,
+                                    cfg.hidden // 128, dev)
+    m = dip_b200.StreamingDIPMlp(L["gate_qw"], L["gate_sc"], L["up_qw"], L["up_sc"], dq, ds,
+                                 shared, cfg.keep_ratio, dev)
+    x = torch.randn(1, 1, cfg.hidden, generator=torch.Generator().manual_seed(3))
+    x = x.to(torch.bfloat16).to(dev)
+    for _ in range(5):
+        m(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        m(x)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps, bool(m._fused)
+
+
 def _time_stack(stack, x0, resid, warmup, steps, dev):
     """Graph-replayed decode steps: warm-up, then `steps` timed with CUDA events."""
     stack.capture()
@@ -761,6 +809,12 @@ def _subresults(args, dev):
     sub.batch, sub.path = 64, "tc"
     out["config3_b64"] = run_config3(sub, emit=False)
     torch.cuda.empty_cache()
+    us, fused = _module_forward_us(dev)
+    out["config0_module_forward"] = {
+        "us_per_call": us, "fused_layer": fused,
+        "what": "StreamingDIPMlp.forward on one config-0 layer, eager (no CUDA graph), "
+                "cold weights only on the first call"}
+    torch.cuda.empty_cache()
     return out
 
 
@@ -787,6 +841,8 @@ def main():
     ap.add_argument("--no-subresults", dest="subresults", action="store_false",
                     help="skip the config-2 and config-3 sub-runs of the one-GPU line")
     ap.add_argument("--sub-steps", type=int, default=8)
+    ap.add_argument("--gemm-tc", type=int, default=0, metavar="N",
+                    help="profiling aid: N launches of the batch-64 tcgen05 gate GEMM, then exit")
     ap.add_argument("--single-layer", type=int, default=0, metavar="N",
                     help="profiling aid: N launches of one config-1 fused layer, then exit")
     ap.add_argument("--path", default="fused", choices=["fused", "chain", "tc", "gather"],
@@ -796,6 +852,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.single_layer:
         run_single_layer(args.single_layer)
+    elif args.gemm_tc:
+        run_gemm_tc(args.gemm_tc)
     elif args.config == 2:
         run_config2(args)
     elif args.config == 3:

@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "../../include/dip_b200.h"
 
@@ -48,6 +49,51 @@ __device__ __forceinline__ void nib8_biased_bf16x2(uint32_t w, uint32_t (&o)[4])
   o[1] = nib_lop3(w >> 4);
   o[2] = nib_lop3(w >> 8);
   o[3] = nib_lop3(w >> 12);
+}
+
+// fp16 variant for the GEMV phases: fp16 has 10 mantissa bits, so the
+// nibbles at bits 4-7 fit without a shift: 0x6400 = 1024.0 (step 1), so
+//   (w & 0x000F000F) ^ 0x64086408 = 1024 + (q + 8)        = q + 1032
+//   (w & 0x00F000F0) ^ 0x64806480 = 1024 + 16 (q + 8)     = 16 (q + 72)
+// and one shift by 8 serves nibbles 2, 3, 6, 7: 5 ALU instructions per 8
+// weights instead of 7 (plus two sub.f16x2 on the FMA pipe, below).  Pairing as nib8_biased_bf16x2: out[p] = (nibble p,
+// nibble p + 4); out[1] and out[3] carry the factor 16.
+constexpr float kNibbleBias16Hi = 72.0f;
+__device__ __forceinline__ uint32_t nib_lop3_f16lo(uint32_t a) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64086408, 0x6a;\n" : "=r"(d) : "r"(a));
+  return d;
+}
+__device__ __forceinline__ uint32_t nib_lop3_f16hi(uint32_t a) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64806480, 0x6a;\n" : "=r"(d) : "r"(a));
+  return d;
+}
+// The low-nibble outputs then have 1032 subtracted exactly (one sub.f16x2
+// each, on the FMA pipe): out[0] and out[2] hold q itself, so no large bias
+// has to cancel after the tensor core's fp32 accumulation; out[1] and out[3]
+// keep 16 (q + 72).
+__device__ __forceinline__ uint32_t sub_f16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ void nib8_biased_f16x2(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t t = w >> 8;
+  const uint32_t k1032 = 0x64086408u;  // (1032.0, 1032.0) in fp16
+  o[0] = sub_f16x2(nib_lop3_f16lo(w), k1032);
+  o[1] = nib_lop3_f16hi(w);
+  o[2] = sub_f16x2(nib_lop3_f16lo(t), k1032);
+  o[3] = nib_lop3_f16hi(t);
+}
+// Warp-level MMA m16n8k16, fp16 x fp16 -> fp32.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // Same idea in fp32: 2^23 = 0x4B000000 has a mantissa step of 1, so

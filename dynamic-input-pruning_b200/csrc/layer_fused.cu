@@ -102,7 +102,8 @@ struct LfGeom {
   static constexpr int lists_bytes = 6 * kLfListMax * 4;
   static constexpr int xs_bytes = (G * 72 * 4 > lists_bytes) ? G * 72 * 4 : lists_bytes;
   static constexpr int gsum = xs + xs_bytes;
-  static constexpr int red = gsum + ((G * 4 + 15) & ~15);  // [tiles][warps][16]
+  // gsum: per group the sums of the even- and odd-indexed x values
+  static constexpr int red = gsum + ((G * 8 + 15) & ~15);  // [tiles][warps][16]
   static constexpr int red_words = (kLfTilesA + 1) * kLfWarps * 16;
   static constexpr int gloc = red + red_words * 4;         // this CTA's g values (bf16)
   static constexpr int lslot = gloc + kLfListMax * 2;      // this CTA's cache slots (CA-DIP)
@@ -195,13 +196,15 @@ __device__ __forceinline__ void lf_tile_dot(const uint8_t* slot, const uint32_t 
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
+      // fp16 operands: the k-high registers (out[1], out[3]) carry 16 x
+      // the weight, and their x fragments 1/16 of x (see the prologue)
       uint32_t qa4[4], qb4[4];
-      nib8_biased_bf16x2(ra[w], qa4);
-      nib8_biased_bf16x2(rb[w], qb4);
+      nib8_biased_f16x2(ra[w], qa4);
+      nib8_biased_f16x2(rb[w], qb4);
       const uint32_t a_even[4] = {qa4[0], qb4[0], qa4[1], qb4[1]};
       const uint32_t a_odd[4] = {qa4[2], qb4[2], qa4[3], qb4[3]};
-      mma_bf16_16816(d0, a_even, xf[gi][4 * w + 0], xf[gi][4 * w + 1]);
-      mma_bf16_16816(d1, a_odd, xf[gi][4 * w + 2], xf[gi][4 * w + 3]);
+      mma_f16_16816(d0, a_even, xf[gi][4 * w + 0], xf[gi][4 * w + 1]);
+      mma_f16_16816(d1, a_odd, xf[gi][4 * w + 2], xf[gi][4 * w + 3]);
     }
     acc_a = fmaf(bf16_bits_to_f32(sca[gi + sofs]), (d0[0] + d1[0]) - bias[gi], acc_a);
     acc_b = fmaf(bf16_bits_to_f32(scb[gi + sofs]), (d0[2] + d1[2]) - bias[gi], acc_b);
@@ -678,31 +681,74 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       __syncthreads();
       inv = misc[32];
     }
-    float part = 0.f;
+    // The GEMV phases run on fp16 operands: x is scaled by 2^m (exact for
+    // a bf16 value above fp16's normal range floor) so that max|x| lands in
+    // [2^13, 2^14), far inside fp16's range whatever the input; the results
+    // are scaled back by 2^-m.  The odd-indexed values of each 8-value word
+    // go to the k-high fragment registers, whose weights carry a factor 16
+    // (nib8_biased_f16x2), so they are scaled by 2^(m-4).
+    uint32_t v4[4] = {0u, 0u, 0u, 0u};
+    float vv[8];
+    float amax = 0.f;
     if (mine) {
-      uint32_t v4[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         v4[q] = a.resid ? ((uint32_t)f32_to_bf16_bits(v[2 * q] * inv) |
                            ((uint32_t)f32_to_bf16_bits(v[2 * q + 1] * inv) << 16))
                         : xa[q];
-        part += bf16_bits_to_f32(v4[q] & 0xFFFF) + bf16_bits_to_f32(v4[q] >> 16);
+        vv[2 * q] = bf16_bits_to_f32(v4[q] & 0xFFFF);
+        vv[2 * q + 1] = bf16_bits_to_f32(v4[q] >> 16);
       }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vv[e]));
       if (a.x_used && b == 1)
         *reinterpret_cast<uint4*>(a.x_used + tid * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
-      uint4 o;
-      o.x = __byte_perm(v4[0], v4[2], 0x5410);
-      o.y = __byte_perm(v4[0], v4[2], 0x7632);
-      o.z = __byte_perm(v4[1], v4[3], 0x5410);
-      o.w = __byte_perm(v4[1], v4[3], 0x7632);
+    }
+    // |x| >= 0: its bit pattern orders like the value
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+    __syncthreads();  // misc (RMSNorm scratch) is reused below
+    if (lane == 0) misc[warp] = amax;
+    __syncthreads();
+    if (tid == 0) {
+      float mx = 0.f;
+      for (int w = 0; w < kLfWarps; ++w) mx = fmaxf(mx, misc[w]);
+      // 2^m with 2^13 <= mx 2^m < 2^14 (m = 0 for zero / non-finite input)
+      int m = 0;
+      if (mx > 0.f && mx <= 3.0e38f) {
+        int e;
+        frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
+        m = max(-100, min(100, 14 - e));
+      }
+      misc[33] = ldexpf(1.f, m);
+      misc[34] = ldexpf(1.f, -m);
+    }
+    __syncthreads();
+    const float sc_lo = misc[33], sc_hi = misc[33] * 0.0625f;
+    float part_e = 0.f, part_o = 0.f;
+    if (mine) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { part_e += vv[2 * q]; part_o += vv[2 * q + 1]; }
+      auto h2 = [](float lo, float hi) {
+        const __half2 p = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&p);
+      };
+      uint4 o;  // values (0,4), (1,5), (2,6), (3,7) of the word
+      o.x = h2(vv[0] * sc_lo, vv[4] * sc_lo);
+      o.y = h2(vv[1] * sc_hi, vv[5] * sc_hi);
+      o.z = h2(vv[2] * sc_lo, vv[6] * sc_lo);
+      o.w = h2(vv[3] * sc_hi, vv[7] * sc_hi);
       const int grp = tid >> 4, t = (tid >> 2) & 3, w = tid & 3;
       *reinterpret_cast<uint4*>(xs + grp * 72 + t * 16 + (t >> 1) * 4 + 4 * w) = o;
     }
-    part += __shfl_xor_sync(0xffffffffu, part, 8);
-    part += __shfl_xor_sync(0xffffffffu, part, 4);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if ((lane & 15) == 0 && mine) gsum[tid >> 4] = part;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      part_e += __shfl_xor_sync(0xffffffffu, part_e, o);
+      part_o += __shfl_xor_sync(0xffffffffu, part_o, o);
+    }
+    if ((lane & 15) == 0 && mine) {
+      gsum[2 * (tid >> 4)] = part_e;
+      gsum[2 * (tid >> 4) + 1] = part_o;
+    }
   }
   __syncthreads();
   uint32_t xf[GW][16];
@@ -716,8 +762,10 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       const uint4 v = bp[q];
       xf[gi][4 * q] = v.x; xf[gi][4 * q + 1] = v.y; xf[gi][4 * q + 2] = v.z; xf[gi][4 * q + 3] = v.w;
     }
-    bias[gi] = kNibbleBias * gsum[grp];
+    // in the 2^m units of the products: sum_even q x + sum_odd (q + 72) x
+    bias[gi] = misc[33] * kNibbleBias16Hi * gsum[2 * grp + 1];
   }
+  const float xinv = misc[34];  // 2^-m: the GEMV sums back in x's units
 
   for (int i = 0; i < nta; ++i) {
     issue_a(i + kLfDepth - 1);
@@ -737,6 +785,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     const int i = r >> 4, row = r & 15;
     float v = 0.f;
     for (int w = 0; w < kLfWarps; ++w) v += red[(i * kLfWarps + w) * 16 + row];
+    v *= xinv;
     const uint16_t o = f32_to_bf16_bits(silu_f32(round_bf16(v)));
     a.g[ra0 + r] = o;
     gloc[r] = o;
@@ -857,6 +906,7 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         const int ti = src >> 4, row = src & 15;
         float v = 0.f;
         for (int w = 0; w < kLfWarps; ++w) v += red[(ti * kLfWarps + w) * 16 + row];
+        v *= xinv;
         h = round_bf16(dh[r] * round_bf16(v));
         if (a.h_out) a.h_out[(TP ? a.c0 : 0) + drow[r]] = f32_to_bf16_bits(h);
         if (r == pad_row) h *= mult;
