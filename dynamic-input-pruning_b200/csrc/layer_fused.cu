@@ -659,9 +659,17 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       v[2 * q] = bf16_bits_to_f32(xa[q] & 0xFFFFu);
       v[2 * q + 1] = bf16_bits_to_f32(xa[q] >> 16);
     }
-    float inv = 1.f;
+    // One block reduction gives both the RMSNorm sum of squares and max |v|.
+    // The GEMV phases run on fp16 operands: x is scaled by 2^m (exact for a
+    // bf16 value above fp16's normal range floor) so that max|x| lands near
+    // [2^13, 2^14) (taken from max|v| * the norm factor; the bf16 rounding of
+    // the normalised values can only move it by one part in 256), far inside
+    // fp16's range whatever the input; the results are scaled back by 2^-m.
+    // The odd-indexed values of each 8-value word go to the k-high fragment
+    // registers, whose weights carry a factor 16 (nib8_biased_f16x2), so they
+    // are scaled by 2^(m-4).
+    float ssq = 0.f, amax = 0.f;
     if (a.resid) {
-      float ssq = 0.f;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         v[2 * q] += bf16_bits_to_f32(ra[q] & 0xFFFFu);
@@ -671,25 +679,41 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       for (int e = 0; e < 8; ++e) ssq = fmaf(v[e], v[e], ssq);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
-      if (lane == 0) misc[warp] = ssq;
-      __syncthreads();
-      if (tid == 0) {
-        float t = 0.f;
-        for (int w = 0; w < kLfWarps; ++w) t += misc[w];
-        misc[32] = rsqrtf(t / (float)H + a.eps);
-      }
-      __syncthreads();
-      inv = misc[32];
     }
-    // The GEMV phases run on fp16 operands: x is scaled by 2^m (exact for
-    // a bf16 value above fp16's normal range floor) so that max|x| lands in
-    // [2^13, 2^14), far inside fp16's range whatever the input; the results
-    // are scaled back by 2^-m.  The odd-indexed values of each 8-value word
-    // go to the k-high fragment registers, whose weights carry a factor 16
-    // (nib8_biased_f16x2), so they are scaled by 2^(m-4).
+    if (mine) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    }
+    // |v| >= 0: its bit pattern orders like the value
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+    if (lane == 0) {
+      misc[warp] = ssq;
+      misc[40 + warp] = amax;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f, mx = 0.f;
+      for (int w = 0; w < kLfWarps; ++w) {
+        t += misc[w];
+        mx = fmaxf(mx, misc[40 + w]);
+      }
+      const float nrm = a.resid ? rsqrtf(t / (float)H + a.eps) : 1.f;
+      mx *= nrm;
+      // 2^m with 2^13 <= mx 2^m < 2^14 (m = 0 for zero / non-finite input)
+      int m = 0;
+      if (mx > 0.f && mx <= 3.0e38f) {
+        int e;
+        frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
+        m = max(-100, min(100, 14 - e));
+      }
+      misc[32] = nrm;
+      misc[33] = ldexpf(1.f, m);
+      misc[34] = ldexpf(1.f, -m);
+    }
+    __syncthreads();
+    const float inv = misc[32];
     uint32_t v4[4] = {0u, 0u, 0u, 0u};
     float vv[8];
-    float amax = 0.f;
     if (mine) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -699,30 +723,9 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         vv[2 * q] = bf16_bits_to_f32(v4[q] & 0xFFFF);
         vv[2 * q + 1] = bf16_bits_to_f32(v4[q] >> 16);
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vv[e]));
       if (a.x_used && b == 1)
         *reinterpret_cast<uint4*>(a.x_used + tid * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
     }
-    // |x| >= 0: its bit pattern orders like the value
-    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
-    __syncthreads();  // misc (RMSNorm scratch) is reused below
-    if (lane == 0) misc[warp] = amax;
-    __syncthreads();
-    if (tid == 0) {
-      float mx = 0.f;
-      for (int w = 0; w < kLfWarps; ++w) mx = fmaxf(mx, misc[w]);
-      // 2^m with 2^13 <= mx 2^m < 2^14 (m = 0 for zero / non-finite input)
-      int m = 0;
-      if (mx > 0.f && mx <= 3.0e38f) {
-        int e;
-        frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
-        m = max(-100, min(100, 14 - e));
-      }
-      misc[33] = ldexpf(1.f, m);
-      misc[34] = ldexpf(1.f, -m);
-    }
-    __syncthreads();
     const float sc_lo = misc[33], sc_hi = misc[33] * 0.0625f;
     float part_e = 0.f, part_o = 0.f;
     if (mine) {
@@ -807,61 +810,24 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // ------------------------------------------------------------ speculation
   // This CTA's nts*16 rows with the largest |g| (about its expected share of
   // k, so nearly all of them end up selected): their up projection starts now,
-  // while the coordinator computes the exact selection.  Warp 0 finds T, the
-  // (nts*16)-th largest key, by a 15-step radix select and lists the rows
-  // (keys > T, then keys == T while places remain, each in row order).
+  // while the coordinator computes the exact selection.  T, the (nts*16)-th
+  // largest key, comes from the CTA's coarse histogram (built with the hash
+  // table below) and a 128-bin histogram of the one coarse bin holding it;
+  // warp 0 then lists the rows (keys > T, then keys == T while places
+  // remain, each in row order).
   int* crow = reinterpret_cast<int*>(smem + Geo::lists);  // C list: spec rows, then rest rows
   int* drow = crow + kLfListMax;         // D list: selected channels
   int* dsrc = drow + kLfListMax;         // D entry -> C list position
   float* dh = reinterpret_cast<float*>(dsrc + kLfListMax);  // D entry: g, then h
   int* cpos = reinterpret_cast<int*>(dh + kLfListMax);      // local row -> C position or -1
   __shared__ int2 warp_tot[33];
-  __shared__ int s_nts;
+  __shared__ int s_nts, s_b1, s_rank;
+  __shared__ unsigned s_fine[128];
   const unsigned my_key = tid < na ? (gloc[tid] & 0x7FFFu) : 0xFFFFu;
   const bool my_valid = my_key <= 0x7F80u;
   if (warp == 0) {
-    constexpr int kPer = (16 * kLfTilesA + 31) / 32;  // rows per lane
-    unsigned key[kPer];
-    int nv = 0;
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      const int r = q * 32 + lane;
-      key[q] = r < na ? (gloc[r] & 0x7FFFu) : 0xFFFFu;
-      if (key[q] > 0x7F80u) key[q] = 0xFFFFu;  // NaN: never speculated
-      nv += key[q] != 0xFFFFu;
-      if (r < na) cpos[r] = -1;
-    }
-    nv = __reduce_add_sync(0xffffffffu, nv);
-    const int nts_w = min(na * K / IT / 16, nv / 16);  // na * K < 2^31 (host check)
-    if (nts_w > 0) {
-      const int nspec = nts_w * 16;
-      unsigned T = 0;
-      for (int bit = 14; bit >= 0; --bit) {
-        const unsigned cand = T | (1u << bit);
-        int c = 0;
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) c += key[q] != 0xFFFFu && key[q] >= cand;
-        if (__reduce_add_sync(0xffffffffu, c) >= nspec) T = cand;
-      }
-      const unsigned lt = (1u << lane) - 1u;
-      int pos = 0;
-#pragma unroll
-      for (int q = 0; q < kPer; ++q) {  // keys > T
-        const bool gt = key[q] != 0xFFFFu && key[q] > T;
-        const unsigned m = __ballot_sync(0xffffffffu, gt);
-        if (gt) { crow[pos + __popc(m & lt)] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = pos + __popc(m & lt); }
-        pos += __popc(m);
-      }
-#pragma unroll
-      for (int q = 0; q < kPer; ++q) {  // keys == T while places remain
-        const bool eq = key[q] == T;
-        const unsigned m = __ballot_sync(0xffffffffu, eq);
-        const int p = pos + __popc(m & lt);
-        if (eq && p < nspec) { crow[p] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = p; }
-        pos += __popc(m);
-      }
-    }
-    if (lane == 0) s_nts = max(nts_w, 0);
+    for (int r = lane; r < na; r += 32) cpos[r] = -1;
+    for (int i = lane; i < 128; i += 32) s_fine[i] = 0u;
   } else if ((warp - 1) * 32 < na) {
     // |g| histograms of this CTA's keys: equal keys are merged in a shared
     // memory hash table first (SiLU's minimum piles ~1/8 of all values onto
@@ -882,7 +848,85 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     }
   }
   __syncthreads();
+  if (warp == 0) {
+    // coarse bins 255 - (8 lane + q), q = 0..7, in descending order
+    int c8[8], loc = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { c8[q] = (int)hcrs[255 - (8 * lane + q)]; loc += c8[q]; }
+    int incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int nv = __shfl_sync(0xffffffffu, incl, 31);  // valid (non-NaN) keys
+    const int nts_w = min(na * K / IT / 16, nv / 16);     // na * K < 2^31 (host check)
+    const int nspec = nts_w * 16;
+    int b1 = -1, above = 0, run = incl - loc;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (nspec > 0 && run < nspec && run + c8[q] >= nspec) { b1 = 255 - (8 * lane + q); above = run; }
+      run += c8[q];
+    }
+    const int bl = __reduce_max_sync(0xffffffffu, b1 + 1) - 1;
+    const int ab = __reduce_max_sync(0xffffffffu, b1 == bl ? above : 0);
+    if (lane == 0) {
+      s_nts = max(nts_w, 0);
+      s_b1 = nts_w > 0 ? bl : -1;
+      s_rank = nspec - ab;  // 1-based rank of T from the top inside bin b1
+    }
+  }
+  __syncthreads();
   const int nts = s_nts;
+  if (s_b1 >= 0 && my_valid && (int)(my_key >> 7) == s_b1) atomicAdd(&s_fine[my_key & 127], 1u);
+  __syncthreads();
+  if (warp == 0 && nts > 0) {
+    const int b1 = s_b1, rank = s_rank, nspec = nts * 16;
+    // fine bins 127 - (4 lane + q), descending
+    int f4[4], loc = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) { f4[q] = (int)s_fine[127 - (4 * lane + q)]; loc += f4[q]; }
+    int incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int f = -1, run = incl - loc;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (run < rank && run + f4[q] >= rank) f = 127 - (4 * lane + q);
+      run += f4[q];
+    }
+    f = __reduce_max_sync(0xffffffffu, f + 1) - 1;
+    const unsigned T = ((unsigned)b1 << 7) | (unsigned)max(f, 0);
+    constexpr int kPer = (16 * kLfTilesA + 31) / 32;  // rows per lane
+    const unsigned lt = (1u << lane) - 1u;
+    unsigned key[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int r = q * 32 + lane;
+      key[q] = r < na ? (gloc[r] & 0x7FFFu) : 0xFFFFu;
+      if (key[q] > 0x7F80u) key[q] = 0xFFFFu;  // NaN: never speculated
+    }
+    int pos = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {  // keys > T
+      const bool gt = key[q] != 0xFFFFu && key[q] > T;
+      const unsigned m = __ballot_sync(0xffffffffu, gt);
+      if (gt) { crow[pos + __popc(m & lt)] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = pos + __popc(m & lt); }
+      pos += __popc(m);
+    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {  // keys == T while places remain
+      const bool eq = key[q] == T;
+      const unsigned m = __ballot_sync(0xffffffffu, eq);
+      const int p = pos + __popc(m & lt);
+      if (eq && p < nspec) { crow[p] = ra0 + q * 32 + lane; cpos[q * 32 + lane] = p; }
+      pos += __popc(m);
+    }
+  }
+  __syncthreads();
 
   // ------------------------------------------------------------ phases C + D
   // One cp.async stream per warp: spec up tiles, rest up tiles (this CTA's
