@@ -691,14 +691,17 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       misc[40 + warp] = amax;
     }
     __syncthreads();
-    if (tid == 0) {
+    // every thread combines the per-warp values itself (same order, same
+    // result everywhere): no second barrier
+    float sc_m, sc_minv, inv;
+    {
       float t = 0.f, mx = 0.f;
       for (int w = 0; w < kLfWarps; ++w) {
         t += misc[w];
         mx = fmaxf(mx, misc[40 + w]);
       }
-      const float nrm = a.resid ? rsqrtf(t / (float)H + a.eps) : 1.f;
-      mx *= nrm;
+      inv = a.resid ? rsqrtf(t / (float)H + a.eps) : 1.f;
+      mx *= inv;
       // 2^m with 2^13 <= mx 2^m < 2^14 (m = 0 for zero / non-finite input)
       int m = 0;
       if (mx > 0.f && mx <= 3.0e38f) {
@@ -706,12 +709,9 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
         frexpf(mx, &e);  // mx = f 2^e, f in [0.5, 1)
         m = max(-100, min(100, 14 - e));
       }
-      misc[32] = nrm;
-      misc[33] = ldexpf(1.f, m);
-      misc[34] = ldexpf(1.f, -m);
+      sc_m = ldexpf(1.f, m);
+      sc_minv = ldexpf(1.f, -m);
     }
-    __syncthreads();
-    const float inv = misc[32];
     uint32_t v4[4] = {0u, 0u, 0u, 0u};
     float vv[8];
     if (mine) {
@@ -726,7 +726,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
       if (a.x_used && b == 1)
         *reinterpret_cast<uint4*>(a.x_used + tid * 8) = make_uint4(v4[0], v4[1], v4[2], v4[3]);
     }
-    const float sc_lo = misc[33], sc_hi = misc[33] * 0.0625f;
+    const float sc_lo = sc_m, sc_hi = sc_m * 0.0625f;
+    if (tid == 0) {
+      misc[33] = sc_m;
+      misc[34] = sc_minv;
+    }
     float part_e = 0.f, part_o = 0.f;
     if (mine) {
 #pragma unroll
@@ -1218,6 +1222,11 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // GW == 1), channel pair l & 7, hi or lo part (l / 8) & 1, so both groups'
   // values come from one pass of the whole warp
   float colsum = 0.f;
+  // The down operands B = h s 2^p run in fp16 hi + lo parts (22 bits).  2^p
+  // is this warp's: set from the first tile's max |h s| so that it lands in
+  // [2^13, 2^14); a later tile that would pass 2^15 lowers it, and the
+  // accumulators and column sums are rescaled by the same exact power of two.
+  float dsc = 0.f;  // 2^p; 0 = not set yet
   const int tpair = lane & 7, twhich = (lane >> 3) & 1, ub = (GW == 2) ? (lane >> 4) : 0;
   for (int j = nC; j < nC + nD; ++j) {
     cp_wait_lf2();
@@ -1227,19 +1236,47 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     const uint8_t* slot = ring + (j % kLfDepth) * Geo::slot;
     const int i = j - nC;
     uint32_t bval = 0;
+    float hs2[2] = {0.f, 0.f}, hmx = 0.f;
     if (GW == 2 || lane < 16) {
-      float v2[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int c = 2 * tpair + e;
         const uint16_t* sp = reinterpret_cast<const uint16_t*>(slot + 16 * kLfDnPitch + c * 4);
         const int sidx = (GW == 1) ? (warp & 1) : ub;
-        const float hs = dh[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
-        const float h1 = round_bf16(hs);
-        v2[e] = twhich ? round_bf16(hs - h1) : h1;
+        hs2[e] = dh[i * 16 + c] * bf16_bits_to_f32(sp[sidx]);
+      }
+      hmx = fmaxf(fabsf(hs2[0]), fabsf(hs2[1]));
+    }
+    // this tile's max |h s| (warp-uniform) and the scale decision
+    hmx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(hmx)));
+    if (hmx > 0.f && hmx <= 3.0e38f && (dsc == 0.f || hmx * dsc >= 32768.f)) {
+      int e;
+      frexpf(hmx, &e);
+      const float nsc = ldexpf(1.f, max(-120, min(120, 14 - e)));
+      if (dsc != 0.f) {  // lower the scale: rescale what is accumulated
+        const float d = nsc / dsc;
+#pragma unroll
+        for (int u = 0; u < GW; ++u)
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+#pragma unroll
+            for (int t = 0; t < 4; ++t) acc[u][m][t] *= d;
+        colsum *= d;
+      }
+      dsc = nsc;
+    }
+    if (GW == 2 || lane < 16) {
+      // B = h s 2^p as fp16 hi + lo
+      float v2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float hs = hs2[e] * dsc;
+        const float h1 = __half2float(__float2half_rn(hs));
+        v2[e] = twhich ? __half2float(__float2half_rn(hs - h1)) : h1;
       }
       colsum += v2[0] + v2[1];
-      bval = (uint32_t)f32_to_bf16_bits(v2[0]) | ((uint32_t)f32_to_bf16_bits(v2[1]) << 16);
+      const __half2 p2 = __floats2half2_rn(v2[0], v2[1]);
+      bval = *reinterpret_cast<const uint32_t*>(&p2);
     }
 #pragma unroll
     for (int u = 0; u < GW; ++u) {
@@ -1257,31 +1294,33 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
                                __byte_perm(r2.y, r3.y, 0x5410), __byte_perm(r2.y, r3.y, 0x7632)};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
+        // rows gq (a[0], a[2]): exact q; rows gq + 8 (a[1], a[3]): 16 (q + 72)
         uint32_t xa[4], xc[4];
-        nib8_biased_bf16x2(pab[q], xa);
-        nib8_biased_bf16x2(pcd[q], xc);
+        nib8_biased_f16x2(pab[q], xa);
+        nib8_biased_f16x2(pcd[q], xc);
         const uint32_t a0[4] = {xa[0], xa[1], xc[0], xc[1]};
         const uint32_t a1[4] = {xa[2], xa[3], xc[2], xc[3]};
-        mma_bf16_16816(acc[u][2 * q], a0, b0, b1);
-        mma_bf16_16816(acc[u][2 * q + 1], a1, b0, b1);
+        mma_f16_16816(acc[u][2 * q], a0, b0, b1);
+        mma_f16_16816(acc[u][2 * q + 1], a1, b0, b1);
       }
     }
     __syncwarp();
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
+  const float dsc_inv = dsc != 0.f ? 1.f / dsc : 1.f;  // exact: a power of two
 #pragma unroll
   for (int u = 0; u < GW; ++u) {
     float cs = colsum;
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-    const float bias_d = kNibbleBias * __shfl_sync(0xffffffffu, cs, 16 * u);
+    const float bias_d = kNibbleBias16Hi * __shfl_sync(0xffffffffu, cs, 16 * u);
     if (tq == 0) {
       float* dst = a.partial + (size_t)b * H + (warp * GW + u) * kGroup + gq * 16;
       float v[16];
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
-        v[2 * m] = acc[u][m][0] + acc[u][m][1] - bias_d;
-        v[2 * m + 1] = acc[u][m][2] + acc[u][m][3] - bias_d;
+        v[2 * m] = (acc[u][m][0] + acc[u][m][1]) * dsc_inv;
+        v[2 * m + 1] = ((acc[u][m][2] + acc[u][m][3]) * 0.0625f - bias_d) * dsc_inv;
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q)
