@@ -109,7 +109,8 @@ struct LfGeom {
   static constexpr int lslot = gloc + kLfListMax * 2;      // this CTA's cache slots (CA-DIP)
   static constexpr int misc = lslot + kLfListMax * 4;      // small scalars
   static constexpr int hist = misc + 256;                  // CTA histogram: hash keys,
-  static constexpr int total = hist + 3 * 256 * 4;         // counts, coarse bins
+  static constexpr int slot64 = hist + 3 * 256 * 4;        // counts, coarse bins; CA: id2slot
+  static constexpr int total = slot64 + kLfListMax * 8;    // of this CTA's rows (int64)
   static_assert(total <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -635,6 +636,13 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
   // Only the first tile goes out ahead of the layer input: the input loads
   // queue behind every line this SM has requested, so the other tiles are
   // requested right after them.
+  // CA-DIP: the cache slots of this CTA's rows travel with the first gate
+  // tile (they are static like the weights); loaded after the gate they held
+  // the whole CTA for a DRAM round trip at the next barrier.
+  if (CA && tid < na)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem + Geo::slot64 + tid * 8)),
+                 "l"(a.id2slot + ra0 + tid)
+                 : "memory");
   issue_a(0);
   pdl_wait();
   read_tag();
@@ -798,11 +806,12 @@ __global__ void __launch_bounds__(kLfThreads, 1) layer_fused_kernel(const LfArgs
     gloc[r] = o;
   }
   {
-    // cache slots of this CTA's rows (-1: no cache), loaded by the threads
-    // the loop above leaves idle
+    // cache slots of this CTA's rows (-1: no cache), narrowed from the
+    // staged int64 values by the threads the loop above leaves idle
     int* lslot_w = reinterpret_cast<int*>(smem + Geo::lslot);
     const int t = tid - (kLfThreads - 16 * kLfTilesA);
-    if (CA && t >= 0 && t < na) lslot_w[t] = (int)a.id2slot[ra0 + t];
+    if (CA && t >= 0 && t < na)
+      lslot_w[t] = (int)reinterpret_cast<const int64_t*>(smem + Geo::slot64)[t];
   }
   unsigned* hkey = reinterpret_cast<unsigned*>(smem + Geo::hist);  // [256] hash slots: key
   unsigned* hcnt = hkey + 256;                                      // [256] its count
